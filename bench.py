@@ -1,0 +1,274 @@
+"""Headline benchmark: Stack training throughput (tokens/s) on B200.
+
+Workload: configs/stack_100m.json (d=1024, 16 heads, block 16,
+``Lx7,G``), random-token task (next-token loss on every position), sequence
+length 8192, batch 1 per data-parallel replica, bf16 autocast with fp32
+master weights and AdamW, Ulysses context parallelism over all N ranks
+(``cpN``). Synthetic data, random-init weights.
+
+Usage::
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        # N > 1
+
+One JSON line from rank 0. ``value`` is the whole-job tokens/s over the K
+timed steps: W untimed warm-up steps, then a barrier + synchronize, CUDA
+events around exactly K steps on every rank, the maximum elapsed time over
+ranks. Every step copies its inputs from pinned host memory and reads its
+loss back; ``e2e`` is the same K steps timed by the host clock (barrier +
+synchronize on both sides), i.e. through the public training API end to
+end. Inputs per step (ids/targets/mask, ~0.14 MB) are smaller than L2, but
+each step streams ~1.3 GB of activations and weights, far larger than the
+126 MB L2, so no explicit flush is needed (``l2`` in the config says so).
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+BASELINE_TOKENS_PER_S = None          # BASELINE.md publishes no B200 number for this config
+METRIC = "train_tokens_per_second"
+CONFIG = ROOT / "configs" / "stack_100m.json"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--length", type=int, default=8192)
+    p.add_argument("--config", default=str(CONFIG))
+    p.add_argument("--cp", type=int, default=0, help="context parallel size (default: all ranks)")
+    p.add_argument("--recompute", action="store_true", help="activation recomputation (same on both arms)")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = set(indices)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.indices:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from exploration_b200 import ExecutionConfig, ParallelContext, build_model
+    from exploration_b200.cli import parse_args as cli_args
+    from exploration_b200.ops import _native
+    from exploration_b200.runtime.engine import Trainer, make_batch
+
+    torch.cuda.set_device(local_rank)
+    cp = args.cp or world
+    argv = ["train", "--config", args.config, "--task", "random", "--length", str(args.length),
+            "--batch-size", "1", "--precision", "bf16", "--backend", "cuda", "--context-parallel", str(cp),
+            "--steps", str(args.warmup + args.steps), "--save", "", "--log-every", "1000000"]
+    argv.append("--checkpoint-chunks" if args.recompute else "--no-checkpoint-chunks")
+    targs = cli_args(argv)
+    parallel = ParallelContext.initialize(cp, "cuda")
+    device = torch.device("cuda", local_rank)
+    torch.manual_seed(0)
+    options = {k: getattr(targs, k) for k in ("vocab_size", "dim", "heads", "block_size", "topk", "arch",
+                                               "ffn_ratio")}
+    execution = ExecutionConfig(backend="cuda", checkpoint_chunks=targs.checkpoint_chunks,
+                                encoder_chunk=targs.encoder_chunk, query_chunk=targs.query_chunk,
+                                loss_chunk=targs.loss_chunk)
+    model = build_model({"model": "stack", **options}, execution=execution, device=device)
+    model.train()
+    trainer = Trainer(targs, model, parallel)
+    ext = _native.load()
+    generator = torch.Generator().manual_seed(100 + parallel.dp_rank)
+    h2d = d2h = 0
+
+    def step(index):
+        nonlocal h2d, d2h
+        trainer.optimizer.zero_grad(set_to_none=True)
+        trainer.set_lr(index)
+        ids, target, mask, _ = make_batch(targs, generator)
+        ids, target, mask = ids.pin_memory(), target.pin_memory(), mask.pin_memory()
+        stats = trainer.micro_step(ids, target, mask, last=True)
+        trainer.finish_step()
+        loss = float(stats[0])                     # device -> host read of the step's result
+        shard = -(-ids.shape[1] // (model.block_size * cp)) * model.block_size
+        h2d = shard * ids.shape[0] * (ids.element_size() + target.element_size() + mask.element_size())
+        d2h = stats.element_size() * stats.numel()
+        return loss
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ext.launch_count()
+    sampler = ClockSampler([local_rank]) if rank == 0 else contextlib.nullcontext()
+    with sampler:
+        wall0 = time.perf_counter()
+        start.record()
+        losses = [step(args.warmup + i) for i in range(args.steps)]
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+    launches = ext.launch_count() - launches0
+    elapsed = torch.tensor([start.elapsed_time(end) / 1e3, wall], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    device_s, wall_s = (float(x) for x in elapsed)
+    tokens = args.steps * parallel.dp_size * args.length          # batch 1 per DP replica
+    result = None
+    if rank == 0:
+        value = tokens / device_s
+        result = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(device_s * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong" if cp > 1 or world == 1 else "weak",
+            "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
+            "dtype": "bf16", "data": "synthetic (uniform random token ids), random-init weights",
+            "config": {"model": "stack_100m", "global_batch": parallel.dp_size, "seq_len": args.length,
+                       "parallelism": f"cp{cp}" + (f"xdp{parallel.dp_size}" if parallel.dp_size > 1 else ""),
+                       "activation_recompute": bool(args.recompute), "optimizer": "fused AdamW fp32 master",
+                       "l2": "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)"},
+            "clocks": sampler.summary(),
+            "e2e": {"value": round(tokens / wall_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": int(launches),
+            "final_loss": round(losses[-1] / max(1, args.length // cp), 4),
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+# ---------------------------------------------------------------------------
+# reference arm (unmodified reference from baseline/_ref, its own public CLI)
+# ---------------------------------------------------------------------------
+
+def run_reference(args, rank, world, local_rank):
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "st" / "__init__.py").exists():
+        return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    # Import the reference's `st` package, not this repository's alias of it.
+    sys.path = [str(ref_root)] + [p for p in sys.path if Path(p or ".").resolve() != ROOT]
+    for name in list(sys.modules):
+        if name == "st" or name.startswith("st."):
+            del sys.modules[name]
+    import st  # noqa: F401  (the reference)
+    from st.cli import main as reference_main
+    cp = args.cp or world
+    argv = ["train", "--config", str(args.config), "--task", "random", "--length", str(args.length),
+            "--batch-size", "1", "--precision", "bf16", "--backend", "auto", "--context-parallel", str(cp),
+            "--steps", str(args.warmup + args.steps), "--log-every", "1", "--save", "", "--eval-every", "0",
+            "--checkpoint-chunks" if args.recompute else "--no-checkpoint-chunks"]
+    buffer = io.StringIO()
+    with contextlib.redirect_stdout(buffer):
+        reference_main(argv)
+    if rank != 0:
+        return None
+    records = [json.loads(line) for line in buffer.getvalue().splitlines() if line.startswith("{")]
+    train = [r for r in records if r.get("event") == "train"][-args.steps:]
+    dp = world // cp
+    tokens_per_step = dp * args.length
+    seconds = sum(tokens_per_step / r["tokens_per_second"] for r in train)
+    value = tokens_per_step * len(train) / seconds
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": len(train), "warmup": args.warmup, "ms_per_step": round(seconds * 1e3 / len(train), 3),
+            "higher_is_better": True, "scaling": "strong" if cp > 1 or world == 1 else "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform random token ids), random-init weights",
+            "config": {"model": "stack_100m", "global_batch": dp, "seq_len": args.length,
+                       "parallelism": f"cp{cp}", "activation_recompute": bool(args.recompute),
+                       "timing": "reference's own per-step host clock after cuda.synchronize, max over ranks"},
+            "peak_allocated_gib": train[-1].get("peak_allocated_gib") if train else None}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    runner = run_reference if args.impl == "reference" else run_ours
+    try:
+        result = runner(args, rank, world, local_rank)
+    except Exception as exc:
+        if args.impl == "reference":
+            result = {"impl": "reference", "unavailable": f"{type(exc).__name__}: {str(exc)[:200]}"}
+        else:
+            raise
+    if rank == 0 and result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

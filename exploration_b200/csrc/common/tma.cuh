@@ -1,0 +1,68 @@
+// Host helpers: TMA tensor maps and the per-device error slot of the
+// bounded-wait protocol (see sm100.cuh).
+#pragma once
+
+#include <ATen/ATen.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "sm100.cuh"
+
+namespace eb {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status);
+    TORCH_CHECK(err == cudaSuccess && status == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "cuTensorMapEncodeTiled is unavailable");
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+// bf16 tensor [B, L, H, D] viewed as (D, H, L, B); boxes of 64 x 1 x rows x 1
+// with 128-byte swizzle (the canonical K-major / MN-major UMMA atom).
+inline CUtensorMap make_bhld_map(void* base, int batch, int length, int heads, int dim, int rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  CUtensorMap map;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(length), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(dim) * 2, static_cast<cuuint64_t>(heads) * dim * 2,
+                           static_cast<cuuint64_t>(length) * heads * dim * 2};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t elem[4] = {1, 1, 1, 1};
+  CUresult res = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, elem,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", static_cast<int>(res));
+  return map;
+}
+
+// Row-major bf16 matrix [rows, cols] (cols contiguous) with boxes of
+// 64 columns x box_rows rows, 128-byte swizzle.
+inline CUtensorMap make_matrix_map(const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
+                                   int box_rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult res = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", static_cast<int>(res));
+  return map;
+}
+
+// One error slot per device, allocated on first use and kept for the process
+// (defined in attention/gated_entry.cu).
+sm100::ErrorSlot* device_error_slot(int device);
+
+}  // namespace eb

@@ -1,0 +1,265 @@
+// LayerNorm (forward/backward) and bias+GELU (forward/backward) for sm_100a.
+//
+// LayerNorm: one warp per row, fp32 statistics; the output is written
+// directly in the matmul dtype (bf16 under autocast), which removes the
+// separate cast kernel autocast would run before the next GEMM. The
+// backward writes dx per row and reduces dgamma/dbeta per column in a
+// second, deterministic pass (no atomics).
+//
+// GELU is the exact erf form of torch.nn.GELU().
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "../common/util.cuh"
+
+namespace eb {
+namespace {
+
+constexpr int kRowWarps = 8;          // rows per CTA for row-wise kernels
+constexpr int kColThreads = 256;      // columns per CTA for column reductions
+constexpr int kColSplits = 148;       // row splits of column reductions (one wave)
+
+template <typename TIn, typename TOut>
+__global__ void __launch_bounds__(kRowWarps * 32)
+layer_norm_fwd_kernel(const TIn* __restrict__ x, const float* __restrict__ w,
+                      const float* __restrict__ b, TOut* __restrict__ y, float* __restrict__ mean,
+                      float* __restrict__ rstd, int rows, int cols, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowWarps + warp;
+  if (row >= rows) return;
+  const TIn* xr = x + static_cast<int64_t>(row) * cols;
+  float sum = 0.f;
+  for (int c = lane; c < cols; c += 32) sum += load_f(xr + c);
+  const float mu = warp_sum(sum) / cols;
+  float sq = 0.f;
+  for (int c = lane; c < cols; c += 32) {
+    float d = load_f(xr + c) - mu;
+    sq += d * d;
+  }
+  const float rs = rsqrtf(warp_sum(sq) / cols + eps);
+  TOut* yr = y + static_cast<int64_t>(row) * cols;
+  for (int c = lane; c < cols; c += 32) yr[c] = cast_f<TOut>((load_f(xr + c) - mu) * rs * w[c] + b[c]);
+  if (lane == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+}
+
+template <typename TIn, typename TGrad>
+__global__ void __launch_bounds__(kRowWarps * 32)
+layer_norm_bwd_dx_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x,
+                         const float* __restrict__ w, const float* __restrict__ mean,
+                         const float* __restrict__ rstd, TIn* __restrict__ dx, int rows, int cols) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowWarps + warp;
+  if (row >= rows) return;
+  const int64_t base = static_cast<int64_t>(row) * cols;
+  const float mu = mean[row], rs = rstd[row];
+  float s1 = 0.f, s2 = 0.f;   // sum(dxhat), sum(dxhat * xhat)
+  for (int c = lane; c < cols; c += 32) {
+    float xh = (load_f(x + base + c) - mu) * rs;
+    float g = load_f(dy + base + c) * w[c];
+    s1 += g;
+    s2 += g * xh;
+  }
+  s1 = warp_sum(s1) / cols;
+  s2 = warp_sum(s2) / cols;
+  for (int c = lane; c < cols; c += 32) {
+    float xh = (load_f(x + base + c) - mu) * rs;
+    float g = load_f(dy + base + c) * w[c];
+    dx[base + c] = cast_f<TIn>(rs * (g - s1 - xh * s2));
+  }
+}
+
+// Column partial sums of dy * xhat and dy over a contiguous range of rows.
+template <typename TIn, typename TGrad>
+__global__ void __launch_bounds__(kColThreads)
+layer_norm_bwd_dwdb_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x,
+                           const float* __restrict__ mean, const float* __restrict__ rstd,
+                           float* __restrict__ part_w, float* __restrict__ part_b, int rows,
+                           int cols, int rows_per_split) {
+  const int c = blockIdx.x * kColThreads + threadIdx.x;
+  const int split = blockIdx.y;
+  if (c >= cols) return;
+  const int r0 = split * rows_per_split, r1 = min(rows, r0 + rows_per_split);
+  float aw = 0.f, ab = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const int64_t i = static_cast<int64_t>(r) * cols + c;
+    float g = load_f(dy + i);
+    aw += g * (load_f(x + i) - mean[r]) * rstd[r];
+    ab += g;
+  }
+  part_w[static_cast<int64_t>(split) * cols + c] = aw;
+  part_b[static_cast<int64_t>(split) * cols + c] = ab;
+}
+
+__global__ void column_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                  int splits, int cols) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float acc = 0.f;
+  for (int s = 0; s < splits; ++s) acc += part[static_cast<int64_t>(s) * cols + c];
+  out[c] = acc;
+}
+
+EB_DEVICE float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
+
+EB_DEVICE float gelu_grad(float v) {
+  const float cdf = 0.5f * (1.f + erff(v * 0.70710678118654752f));
+  const float pdf = expf(-0.5f * v * v) * 0.39894228040143268f;
+  return cdf + v * pdf;
+}
+
+template <typename T>
+__global__ void bias_gelu_fwd_kernel(const T* __restrict__ h, const float* __restrict__ bias,
+                                     T* __restrict__ out, int64_t total, int cols) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    out[i] = cast_f<T>(gelu(load_f(h + i) + bias[i % cols]));
+  }
+}
+
+// dh = dout * gelu'(h + bias), written per element; column partials of dh for dbias.
+template <typename T>
+__global__ void __launch_bounds__(kColThreads)
+bias_gelu_bwd_kernel(const T* __restrict__ dout, const T* __restrict__ h,
+                     const float* __restrict__ bias, T* __restrict__ dh,
+                     float* __restrict__ part, int rows, int cols, int rows_per_split) {
+  const int c = blockIdx.x * kColThreads + threadIdx.x;
+  const int split = blockIdx.y;
+  if (c >= cols) return;
+  const int r0 = split * rows_per_split, r1 = min(rows, r0 + rows_per_split);
+  const float bc = bias[c];
+  float acc = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const int64_t i = static_cast<int64_t>(r) * cols + c;
+    const float g = load_f(dout + i) * gelu_grad(load_f(h + i) + bc);
+    const T q = cast_f<T>(g);
+    dh[i] = q;
+    acc += g;
+  }
+  part[static_cast<int64_t>(split) * cols + c] = acc;
+}
+
+int row_splits(int rows) { return std::max(1, std::min(kColSplits, rows)); }
+
+}  // namespace
+
+#define EB_DISPATCH_FLOAT_BF16(TYPE, NAME, ...)                                  \
+  [&] {                                                                         \
+    if ((TYPE) == at::kFloat) {                                                 \
+      using NAME = float;                                                       \
+      return __VA_ARGS__();                                                     \
+    } else if ((TYPE) == at::kBFloat16) {                                       \
+      using NAME = __nv_bfloat16;                                               \
+      return __VA_ARGS__();                                                     \
+    }                                                                           \
+    TORCH_CHECK(false, "expected float32 or bfloat16, got ", (TYPE));           \
+  }()
+
+std::vector<at::Tensor> layer_norm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b,
+                                       double eps, at::ScalarType out_dtype) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "x must be contiguous CUDA [T, C]");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && b.scalar_type() == at::kFloat, "fp32 affine params");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rows = x.size(0), cols = x.size(1);
+  auto y = at::empty({rows, cols}, x.options().dtype(out_dtype));
+  auto mean = at::empty({rows}, x.options().dtype(at::kFloat));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, mean, rstd};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int grid = cdiv(rows, kRowWarps);
+  EB_DISPATCH_FLOAT_BF16(x.scalar_type(), TIn, [&] {
+    EB_DISPATCH_FLOAT_BF16(out_dtype, TOut, [&] {
+      layer_norm_fwd_kernel<TIn, TOut><<<grid, kRowWarps * 32, 0, stream>>>(
+          reinterpret_cast<const TIn*>(x.data_ptr()), w.data_ptr<float>(), b.data_ptr<float>(),
+          reinterpret_cast<TOut*>(y.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+          rows, cols, static_cast<float>(eps));
+    });
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(1);
+  return {y, mean, rstd};
+}
+
+std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                       const at::Tensor& mean, const at::Tensor& rstd) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.sizes() == x.sizes(), "dy/x mismatch");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rows = x.size(0), cols = x.size(1);
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({cols}, x.options().dtype(at::kFloat));
+  auto db = at::zeros({cols}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dw, db};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int splits = row_splits(rows);
+  const int per_split = cdiv(rows, splits);
+  auto part_w = at::empty({splits, cols}, x.options().dtype(at::kFloat));
+  auto part_b = at::empty({splits, cols}, x.options().dtype(at::kFloat));
+  EB_DISPATCH_FLOAT_BF16(x.scalar_type(), TIn, [&] {
+    EB_DISPATCH_FLOAT_BF16(dy.scalar_type(), TGrad, [&] {
+      layer_norm_bwd_dx_kernel<TIn, TGrad><<<cdiv(rows, kRowWarps), kRowWarps * 32, 0, stream>>>(
+          reinterpret_cast<const TGrad*>(dy.data_ptr()), reinterpret_cast<const TIn*>(x.data_ptr()),
+          w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+          reinterpret_cast<TIn*>(dx.data_ptr()), rows, cols);
+      dim3 grid(cdiv(cols, kColThreads), splits);
+      layer_norm_bwd_dwdb_kernel<TIn, TGrad><<<grid, kColThreads, 0, stream>>>(
+          reinterpret_cast<const TGrad*>(dy.data_ptr()), reinterpret_cast<const TIn*>(x.data_ptr()),
+          mean.data_ptr<float>(), rstd.data_ptr<float>(), part_w.data_ptr<float>(),
+          part_b.data_ptr<float>(), rows, cols, per_split);
+    });
+  });
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_w.data_ptr<float>(), dw.data_ptr<float>(),
+                                                         splits, cols);
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_b.data_ptr<float>(), db.data_ptr<float>(),
+                                                         splits, cols);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(4);
+  return {dx, dw, db};
+}
+
+at::Tensor bias_gelu_fwd(const at::Tensor& h, const at::Tensor& bias) {
+  TORCH_CHECK(h.is_contiguous() && h.dim() == 2 && bias.scalar_type() == at::kFloat, "bad bias_gelu args");
+  const c10::cuda::CUDAGuard guard(h.device());
+  auto out = at::empty_like(h);
+  const int64_t total = h.numel();
+  if (total == 0) return out;
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(total, 256), 148 * 16));
+  EB_DISPATCH_FLOAT_BF16(h.scalar_type(), T, [&] {
+    bias_gelu_fwd_kernel<T><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const T*>(h.data_ptr()), bias.data_ptr<float>(),
+        reinterpret_cast<T*>(out.data_ptr()), total, static_cast<int>(h.size(1)));
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(1);
+  return out;
+}
+
+std::vector<at::Tensor> bias_gelu_bwd(const at::Tensor& dout, const at::Tensor& h, const at::Tensor& bias) {
+  TORCH_CHECK(dout.sizes() == h.sizes() && dout.is_contiguous() && h.is_contiguous(), "bad shapes");
+  TORCH_CHECK(dout.scalar_type() == h.scalar_type(), "dout/h dtype mismatch");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int rows = h.size(0), cols = h.size(1);
+  auto dh = at::empty_like(h);
+  auto dbias = at::zeros({cols}, h.options().dtype(at::kFloat));
+  if (rows == 0) return {dh, dbias};
+  const int splits = row_splits(rows);
+  auto part = at::empty({splits, cols}, h.options().dtype(at::kFloat));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  EB_DISPATCH_FLOAT_BF16(h.scalar_type(), T, [&] {
+    dim3 grid(cdiv(cols, kColThreads), splits);
+    bias_gelu_bwd_kernel<T><<<grid, kColThreads, 0, stream>>>(
+        reinterpret_cast<const T*>(dout.data_ptr()), reinterpret_cast<const T*>(h.data_ptr()),
+        bias.data_ptr<float>(), reinterpret_cast<T*>(dh.data_ptr()), part.data_ptr<float>(), rows,
+        cols, cdiv(rows, splits));
+  });
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part.data_ptr<float>(), dbias.data_ptr<float>(),
+                                                         splits, cols);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(2);
+  return {dh, dbias};
+}
+
+}  // namespace eb

@@ -31,9 +31,9 @@ MAX_BLOCK = 128
 
 
 def native_supported(q: torch.Tensor, block_size: int) -> bool:
-    return (q.is_cuda and q.dtype in (torch.float32, torch.bfloat16, torch.float16)
-            and 2 <= block_size <= MAX_BLOCK and q.shape[-1] <= MAX_HEAD_DIM
-            and q.shape[-1] % 2 == 0)
+    return (q.is_cuda and q.dtype in (torch.float32, torch.bfloat16)
+            and 2 <= block_size <= MAX_BLOCK and block_size & (block_size - 1) == 0
+            and q.shape[-1] <= MAX_HEAD_DIM and q.shape[-1] % 2 == 0)
 
 
 class _ReferenceGated(torch.autograd.Function):
@@ -93,8 +93,8 @@ def dense_attention(q, k, v, positions, block_size, backend="auto", q_chunk=128,
         if native_supported(q, block_size) and q.dtype == k.dtype == v.dtype:
             return _NativeGated.apply(q, k, v, positions, block_size)
         if path == "cuda":
-            raise ValueError("native gated attention needs matching fp32/bf16/fp16 q/k/v, "
-                             f"head_dim <= {MAX_HEAD_DIM} (even) and 2 <= block_size <= {MAX_BLOCK}")
+            raise ValueError("native gated attention needs matching fp32/bf16 q/k/v, head_dim "
+                             f"<= {MAX_HEAD_DIM} (even) and a power-of-two block size <= {MAX_BLOCK}")
     elif path == "cuda":
         raise ValueError("the native backend runs on CUDA tensors")
     # Autograd Function bodies run outside autocast, so the reference

@@ -39,18 +39,22 @@ def use_native(x: torch.Tensor, backend: str, cdt: torch.dtype) -> bool:
     return x.is_cuda and backend != "torch" and cdt in (torch.bfloat16, torch.float32)
 
 
-_cast_cache: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+# id(param) -> (weak reference to param, {dtype: (param version, copy)}). Tensors
+# define elementwise ``==``, so they cannot be keys of a WeakKeyDictionary.
+_cast_cache: dict = {}
 
 
 def _cached_copy(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    slot = _cast_cache.get(param)
-    if slot is None:
-        slot = _cast_cache[param] = {}
-    hit = slot.get(dtype)
+    key = id(param)
+    entry = _cast_cache.get(key)
+    if entry is None or entry[0]() is not param:
+        entry = (weakref.ref(param, lambda _ref, k=key: _cast_cache.pop(k, None)), {})
+        _cast_cache[key] = entry
+    hit = entry[1].get(dtype)
     if hit is not None and hit[0] == param._version:
         return hit[1]
     value = param.detach().to(dtype)
-    slot[dtype] = (param._version, value)
+    entry[1][dtype] = (param._version, value)
     return value
 
 
@@ -251,9 +255,10 @@ class _LocalAttentionNative(torch.autograd.Function):
 
 def local_attention(qkv, qkv_prev, start, valid_start, n, block, heads, backend="auto"):
     """Windowed causal attention of one block-aligned chunk; returns ``[B, n, H*D]``."""
-    if qkv.is_cuda and backend != "torch" and qkv.dtype in (torch.bfloat16, torch.float32) \
-            and block <= 128 and qkv.shape[-1] <= 256:
-        return _LocalAttentionNative.apply(qkv, qkv_prev, start, valid_start, n, block)
+    if qkv.is_cuda and backend != "torch" and qkv.dtype in (torch.bfloat16, torch.float32):
+        ext = _native.native(qkv)
+        if ext.local_attention_supported(block, qkv.shape[-1]):
+            return _LocalAttentionNative.apply(qkv, qkv_prev, start, valid_start, n, block)
     return local_attention_reference(qkv, qkv_prev, start, valid_start, n, block, heads)
 
 
