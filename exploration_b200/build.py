@@ -31,6 +31,7 @@ SOURCES = [
     "attention/gated_tc.cu",
     "attention/gated_tc_bwd.cu",
     "sparse/sparse_read.cu",
+    "gemm/gemm_tc.cu",
 ]
 
 CUDA_FLAGS = [

@@ -43,6 +43,10 @@ std::vector<at::Tensor> gated_attention_bwd(const at::Tensor& grad, const at::Te
                                             const at::Tensor& lse, int64_t block);
 std::vector<at::Tensor> block_scores_topk(const at::Tensor& q, const at::Tensor& k, const at::Tensor& pos,
                                           int64_t block, int64_t first, int64_t topk);
+bool gemm_supported(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn);
+void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
+          double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial);
 std::vector<at::Tensor> sparse_pop(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                    const at::Tensor& pos, const at::Tensor& ids, const at::Tensor& scores,
                                    const at::Tensor& log_zr, int64_t block, int64_t offset);
@@ -78,6 +82,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_attention_bwd", &eb::gated_attention_bwd);
   m.def("block_scores_topk", &eb::block_scores_topk);
   m.def("sparse_pop", &eb::sparse_pop);
+  m.def("gemm_supported", &eb::gemm_supported);
+  m.def("gemm", &eb::gemm, "persistent tcgen05 GEMM with fused epilogues");
   m.def("launch_count", &eb::launch_count, "kernels launched by this extension so far");
   m.def("device_errors", &device_errors, "read and clear (site, cta) of the last bounded-wait timeout");
 }
