@@ -28,6 +28,10 @@
 #include "../common/sm100.cuh"
 #include "../common/tma.cuh"
 #include "gated_common.cuh"
+#include "gated_noalloc.h"
+
+#include <cstdio>
+#include <mutex>
 
 namespace eb {
 namespace {
@@ -696,3 +700,149 @@ void gated_bwd_tc_launch(const at::Tensor& grad, const at::Tensor& q, const at::
 }
 
 }  // namespace eb
+
+// ===========================================================================
+// No-allocation entry point
+// ===========================================================================
+//
+// Declared in gated_noalloc.h. This entry point has no counterpart in the
+// reference framework; it exists for callers that must not allocate device
+// memory: code running inside a custom allocator or memory pool callback,
+// real-time or embedded hosts that pre-reserve all memory up front, and
+// runtimes that forbid cudaMalloc after start-up (for example while other
+// work is being recorded into a stream). Such callers cannot use
+// gated_attention_bwd above, because that path allocates its per-row scratch
+// (delta, rho) and per-tile position bounds with the PyTorch allocator.
+//
+// Here that scratch lives in one file-scope device array of fixed size.
+// Limits: batch * queries * heads <= kNoAllocMaxRows and
+// batch * ceil(queries / 128) <= kNoAllocMaxTiles; larger calls are rejected
+// with an error message. Every GPU that loads this library keeps the array
+// (about 4.2 MiB) resident until the process exits. All calls on a device
+// share it and it keeps the previous call's contents, so calls whose GPU work
+// may overlap (for example calls on two streams of one device) race on it;
+// the caller must serialise them.
+namespace eb {
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = int64_t(1) << 19;    // delta + rho: 2 x 2 MiB
+constexpr int64_t kNoAllocMaxTiles = int64_t(1) << 14;   // bounds: 192 KiB
+constexpr size_t kNoAllocRowBytes = sizeof(float) * kNoAllocMaxRows;
+constexpr size_t kNoAllocBoundBytes = sizeof(int) * 3 * kNoAllocMaxTiles;
+constexpr size_t kNoAllocBytes = 2 * kNoAllocRowBytes + kNoAllocBoundBytes + 256;
+
+// The scratch array. In host code this name is only a stand-in, never a
+// device address: the host takes the address with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocBytes];
+
+std::mutex noalloc_lock;
+unsigned char* noalloc_base[64] = {nullptr};
+
+int noalloc_fail(char* msg, int cap, const char* text, int code) {
+  if (msg != nullptr && cap > 0) {
+    std::snprintf(msg, static_cast<size_t>(cap), "%s", text);
+  }
+  return code;
+}
+
+// Set-up, once per device, with that device current (the caller's current
+// device): look up the device address of the scratch array.
+int noalloc_scratch_address(int device, unsigned char** out, char* msg, int cap) {
+  std::lock_guard<std::mutex> guard(noalloc_lock);
+  if (noalloc_base[device] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&ptr, noalloc_scratch);
+    if (rc != cudaSuccess || ptr == nullptr) {
+      char text[256];
+      std::snprintf(text, sizeof(text), "cudaGetSymbolAddress(noalloc_scratch) failed: %s",
+                    cudaGetErrorString(rc));
+      return noalloc_fail(msg, cap, text, 2);
+    }
+    noalloc_base[device] = static_cast<unsigned char*>(ptr);
+  }
+  *out = noalloc_base[device];
+  return 0;
+}
+
+template <int D, int B>
+void noalloc_launch(const void* grad, const void* q, const void* k, const void* v, int batch, int queries,
+                    int keys, int heads, const BwdParams& params, cudaStream_t stream) {
+  CUtensorMap tq = make_bhld_map(const_cast<void*>(q), batch, queries, heads, D, kT);
+  CUtensorMap tg = make_bhld_map(const_cast<void*>(grad), batch, queries, heads, D, kT);
+  CUtensorMap tk = make_bhld_map(const_cast<void*>(k), batch, keys, heads, D, kT);
+  CUtensorMap tv = make_bhld_map(const_cast<void*>(v), batch, keys, heads, D, kT);
+  const size_t smem_q = sizeof(DqSmem<D>) + 1024, smem_kv = sizeof(DkvSmem<D>) + 1024;
+  cudaFuncSetAttribute(gated_dq_tc_kernel<D, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+  cudaFuncSetAttribute(gated_dkv_tc_kernel<D, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+  gated_dq_tc_kernel<D, B><<<dim3((queries + kT - 1) / kT, heads, batch), kThreads, smem_q, stream>>>(
+      tq, tg, tk, tv, params);
+  gated_dkv_tc_kernel<D, B><<<dim3((keys + kT - 1) / kT, heads, batch), kThreads, smem_kv, stream>>>(
+      tq, tg, tk, tv, params);
+}
+
+}  // namespace
+}  // namespace eb
+
+extern "C" int eb_gated_attention_bwd_noalloc(const void* grad, const void* q, const void* k, const void* v,
+                                              const int* pos, const void* out, const float* rc, const float* pr,
+                                              const float* zr, const float* lse, void* dq, void* dk, void* dv,
+                                              int batch, int queries, int keys, int heads, int head_dim,
+                                              int block, void* stream_handle, char* error_message,
+                                              int error_capacity) {
+  using namespace eb;
+  char* msg = error_message;
+  const int cap = error_capacity;
+  if (batch < 1 || queries < 1 || keys < 1 || heads < 1)
+    return noalloc_fail(msg, cap, "sizes must be positive", 1);
+  if (!((head_dim == 64 || head_dim == 128) && (block == 16 || block == 32 || block == 64 || block == 128)))
+    return noalloc_fail(msg, cap, "unsupported shape: head_dim must be 64 or 128 and block 16/32/64/128", 1);
+  const int64_t rows = static_cast<int64_t>(batch) * queries * heads;
+  const int q_tiles = (queries + kT - 1) / kT;
+  if (rows > kNoAllocMaxRows) {
+    char text[192];
+    std::snprintf(text, sizeof(text), "batch*queries*heads = %lld exceeds the scratch limit %lld",
+                  static_cast<long long>(rows), static_cast<long long>(kNoAllocMaxRows));
+    return noalloc_fail(msg, cap, text, 1);
+  }
+  if (static_cast<int64_t>(batch) * q_tiles > kNoAllocMaxTiles)
+    return noalloc_fail(msg, cap, "batch * ceil(queries/128) exceeds the scratch tile limit", 1);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    return noalloc_fail(msg, cap, "no current CUDA device", 2);
+  unsigned char* base = nullptr;
+  if (int rc_setup = noalloc_scratch_address(device, &base, msg, cap)) return rc_setup;
+  auto* delta = reinterpret_cast<float*>(base);
+  auto* rho = reinterpret_cast<float*>(base + kNoAllocRowBytes);
+  auto* bounds = reinterpret_cast<int*>(base + 2 * kNoAllocRowBytes);
+  auto* err = reinterpret_cast<sm100::ErrorSlot*>(base + 2 * kNoAllocRowBytes + kNoAllocBoundBytes);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  // delta, rho and bounds are fully rewritten below; only the error slot must start at zero.
+  if (cudaMemsetAsync(err, 0, sizeof(sm100::ErrorSlot), stream) != cudaSuccess)
+    return noalloc_fail(msg, cap, "cudaMemsetAsync of the error slot failed", 2);
+  delta_rho_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(grad), static_cast<const __nv_bfloat16*>(out), rc, pr, delta, rho, rows,
+      head_dim);
+  switch (block) {
+    case 16: tile_bounds_kernel<16><<<dim3(q_tiles, batch), kT, 0, stream>>>(pos, bounds, queries, q_tiles); break;
+    case 32: tile_bounds_kernel<32><<<dim3(q_tiles, batch), kT, 0, stream>>>(pos, bounds, queries, q_tiles); break;
+    case 64: tile_bounds_kernel<64><<<dim3(q_tiles, batch), kT, 0, stream>>>(pos, bounds, queries, q_tiles); break;
+    default: tile_bounds_kernel<128><<<dim3(q_tiles, batch), kT, 0, stream>>>(pos, bounds, queries, q_tiles); break;
+  }
+  BwdParams params{pos, lse, zr, delta, rho, bounds,
+                   static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv),
+                   err, queries, keys, heads, q_tiles,
+                   static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim))),
+                   static_cast<float>(kLog2e / std::sqrt(static_cast<double>(head_dim)))};
+  try {
+#define EB_NOALLOC_CASE(DD, BB) \
+    if (head_dim == DD && block == BB) noalloc_launch<DD, BB>(grad, q, k, v, batch, queries, keys, heads, params, stream);
+    EB_NOALLOC_CASE(64, 16) EB_NOALLOC_CASE(64, 32) EB_NOALLOC_CASE(64, 64) EB_NOALLOC_CASE(64, 128)
+    EB_NOALLOC_CASE(128, 16) EB_NOALLOC_CASE(128, 32) EB_NOALLOC_CASE(128, 64) EB_NOALLOC_CASE(128, 128)
+#undef EB_NOALLOC_CASE
+  } catch (const std::exception& exc) {   // tensor-map encoding rejected an operand
+    return noalloc_fail(msg, cap, exc.what(), 3);
+  }
+  const cudaError_t launched = cudaGetLastError();
+  if (launched != cudaSuccess) return noalloc_fail(msg, cap, cudaGetErrorString(launched), 2);
+  return 0;
+}
