@@ -26,6 +26,7 @@ SOURCES = [
     "fused/norm_act.cu",
     "fused/loss_optim.cu",
     "attention/local_halo.cu",
+    "attention/local_halo_b16.cu",
     "attention/gated_entry.cu",
     "attention/gated_simt.cu",
     "attention/gated_tc.cu",

@@ -318,6 +318,13 @@ std::pair<at::Tensor, at::Tensor> rope_tables(int block, int dim, const at::Devi
 
 }  // namespace
 
+bool local16_supported(int block, int dim);
+std::vector<at::Tensor> local16_fwd_launch(const at::Tensor& qkv, const c10::optional<at::Tensor>& prev,
+                                           int64_t start, int64_t valid_start, int64_t n);
+std::vector<at::Tensor> local16_bwd_launch(const at::Tensor& dout, const at::Tensor& qkv,
+                                           const c10::optional<at::Tensor>& prev, const at::Tensor& out,
+                                           const at::Tensor& lse, int64_t start, int64_t valid_start, int64_t n);
+
 bool local_attention_supported(int block, int dim) {
   return block >= 1 && block <= 128 && dim % 2 == 0 && dim <= 256 && bwd_smem(block, dim) <= 200 * 1024;
 }
@@ -329,6 +336,7 @@ std::vector<at::Tensor> local_attention_fwd(const at::Tensor& qkv, const c10::op
   const int batch = qkv.size(0), heads = qkv.size(3), dim = qkv.size(4);
   TORCH_CHECK(local_attention_supported(block, dim), "unsupported local attention shape");
   const c10::cuda::CUDAGuard guard(qkv.device());
+  if (local16_supported(block, dim) && n > 0) return local16_fwd_launch(qkv, prev, start, valid_start, n);
   auto tables = rope_tables(block, dim, qkv.device());
   LocalArgs a{qkv.data_ptr(), prev.has_value() ? prev->data_ptr() : nullptr, tables.first.data_ptr<float>(),
               tables.second.data_ptr<float>(), static_cast<int>(n), heads, dim, static_cast<int>(block),
@@ -362,6 +370,8 @@ std::vector<at::Tensor> local_attention_bwd(const at::Tensor& dout, const at::Te
   TORCH_CHECK(dout.is_contiguous() && dout.sizes() == out.sizes(), "dout must match out");
   const int batch = qkv.size(0), heads = qkv.size(3), dim = qkv.size(4);
   const c10::cuda::CUDAGuard guard(qkv.device());
+  if (local16_supported(block, dim) && n > 0)
+    return local16_bwd_launch(dout, qkv, prev, out, lse, start, valid_start, n);
   auto tables = rope_tables(block, dim, qkv.device());
   LocalArgs a{qkv.data_ptr(), prev.has_value() ? prev->data_ptr() : nullptr, tables.first.data_ptr<float>(),
               tables.second.data_ptr<float>(), static_cast<int>(n), heads, dim, static_cast<int>(block),

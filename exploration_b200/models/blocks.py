@@ -103,9 +103,9 @@ class HaloMemoryBlock(nn.Module):
         halo = None if previous is None else \
             self._project(previous).view(batch, b, 3, self.heads, self.hd)
         context = fused.local_attention(qkv, halo, start, valid_start, n, b, self.heads, self.backend)
-        y = x + fused.linear(context, self.out, self.backend)
-        return y + fused.feed_forward(fused.layer_norm(y, self.ffn_norm, self.backend), self.ffn,
-                                      self.backend)
+        y = fused.linear_residual(context, self.out, x, self.backend)
+        return fused.ffn_residual(fused.layer_norm(y, self.ffn_norm, self.backend), y, self.ffn,
+                                  self.backend)
 
     def chunk_tokens(self, x) -> int:
         step = self.query_chunk_size * self.block_size

@@ -184,9 +184,9 @@ class StackModel(nn.Module):
         return fused.linear(fused.layer_norm(z, rd.q_norm, self.backend), rd.wq, self.backend)
 
     def _finish(self, rd, z, context):
-        z = z + fused.linear(context, rd.read_out, self.backend)
-        return z + fused.feed_forward(fused.layer_norm(z, rd.ffn_norm, self.backend), rd.ffn,
-                                      self.backend)
+        z = fused.linear_residual(context, rd.read_out, z, self.backend)
+        return fused.ffn_residual(fused.layer_norm(z, rd.ffn_norm, self.backend), z, rd.ffn,
+                                  self.backend)
 
     def _dense_round(self, rd, z, k, v, positions, parallel):
         recompute = self.checkpoint_chunks and torch.is_grad_enabled()
@@ -206,7 +206,7 @@ class StackModel(nn.Module):
 
     def _head_loss(self, hidden, labels):
         h = fused.layer_norm(hidden, self.final_norm, self.backend)
-        logits = fused.linear(h, self.lm_head, self.backend).float()
+        logits = fused.linear(h, self.lm_head, self.backend, out_f32=True)
         return fused.cross_entropy_sum(logits, labels, self.backend)
 
     def forward_loss(self, input_ids, targets, sup=None, parallel=None, offset=0):

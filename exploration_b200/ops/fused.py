@@ -20,7 +20,7 @@ import weakref
 import torch
 from torch.nn import functional as F
 
-from . import _native
+from . import _native, gemm
 from .launch import record
 
 # ----------------------------------------------------------------------------
@@ -125,13 +125,37 @@ def layer_norm(x, norm: torch.nn.LayerNorm, backend: str = "auto"):
 # ----------------------------------------------------------------------------
 
 
-def linear(x, layer: torch.nn.Linear, backend: str = "auto"):
+def linear(x, layer: torch.nn.Linear, backend: str = "auto", out_f32: bool = False):
+    """``layer(x)`` (no-bias layers on the tcgen05 GEMM when native)."""
     cdt = compute_dtype(x, layer.weight.dtype)
     if use_native(x, backend, cdt):
+        if cdt == torch.bfloat16 and layer.bias is None and gemm.usable(x.to(cdt), layer):
+            return gemm.Linear.apply(x.to(cdt), layer.weight, out_f32)
         w = cast_param(layer.weight, cdt)
         b = None if layer.bias is None else cast_param(layer.bias, cdt)
-        return F.linear(x.to(cdt), w, b)
-    return layer(x)
+        out = F.linear(x.to(cdt), w, b)
+        return out.float() if out_f32 else out
+    out = layer(x)
+    return out.float() if out_f32 else out
+
+
+def linear_residual(x, layer: torch.nn.Linear, residual, backend: str = "auto"):
+    """``residual + layer(x)``; on the native path one GEMM whose epilogue adds the fp32 residual."""
+    cdt = compute_dtype(x, layer.weight.dtype)
+    if use_native(x, backend, cdt) and cdt == torch.bfloat16 and residual.dtype == torch.float32 \
+            and gemm.usable(x.to(cdt), layer):
+        return gemm.LinearResidual.apply(x.to(cdt), layer.weight, layer.bias, residual)
+    return residual + linear(x, layer, backend)
+
+
+def ffn_residual(h, y, ffn: torch.nn.Sequential, backend: str = "auto"):
+    """``y + ffn(h)``: two GEMMs with bias+GELU and bias+residual epilogues when native."""
+    up, down = ffn[0], ffn[2]
+    cdt = compute_dtype(h, up.weight.dtype)
+    if use_native(h, backend, cdt) and cdt == torch.bfloat16 and y.dtype == torch.float32 \
+            and gemm.usable(h.to(cdt), up, down):
+        return gemm.FFNResidual.apply(h.to(cdt), y, up.weight, up.bias, down.weight, down.bias)
+    return y + feed_forward(h, ffn, backend)
 
 
 class _BiasGeluNative(torch.autograd.Function):

@@ -1,10 +1,10 @@
 """Linear layers on the persistent tcgen05 GEMM (``csrc/gemm/gemm_tc.cu``).
 
-All three GEMMs of a layer run on the same kernel without transposing any
-tensor: ``y = x W^T`` (both operands K-major), ``dx = dy W`` (W read
-MN-major) and ``dW = dy^T x`` (both read MN-major, fp32 output for the fp32
-master gradient). The fused layers keep elementwise work inside the GEMM
-epilogues:
+The kernel reads either operand K-major or MN-major, so every GEMM of a
+layer runs without a transpose copy. GEMMs that carry an epilogue run on
+it; plain ones with no fusion (``dx = dy W`` and the weight gradients
+``dW = dy^T x`` in fp32) are library GEMMs. The fused layers keep
+elementwise work inside the GEMM epilogues:
 
 * ``linear_residual``: ``out = residual + x W^T (+ b)`` in fp32 (the residual
   stream update), one kernel instead of GEMM + add;
@@ -44,6 +44,16 @@ def gemm(a, a_mn, b, b_mn, out, epilogue, alpha=1.0, bias=None, residual=None, a
     return out
 
 
+def weight_grad(g, x):
+    """``dW = g^T x`` in fp32: a plain GEMM with no epilogue, left to cuBLAS.
+
+    Weight gradients have few output tiles and a long reduction (tokens), a
+    shape where cuBLAS's split reduction is faster than this kernel's
+    one-tile-per-CTA schedule.
+    """
+    return torch.mm(g.t(), x, out_dtype=torch.float32)
+
+
 def _bf16_weight(param):
     from .fused import _cached_copy
     return _cached_copy(param, torch.bfloat16)
@@ -54,15 +64,15 @@ def _flat(x):
 
 
 class Linear(torch.autograd.Function):
-    """``y = x W^T`` with bf16 (or fp32 for ``out_f32``) output; no bias."""
+    """``y = x W^T`` (bf16, or fp32 for ``out_f32``), no bias; fp32 weight gradient."""
 
     @staticmethod
     def forward(ctx, x, weight, out_f32):
+        # No epilogue to fuse: a library GEMM (fp32 output straight from bf16
+        # operands when asked, e.g. for the logits).
         x2 = _flat(x)
         w = _bf16_weight(weight)
-        out = torch.empty(x2.shape[0], w.shape[0], device=x.device,
-                          dtype=torch.float32 if out_f32 else torch.bfloat16)
-        gemm(x2, False, w, False, out, STORE_F32 if out_f32 else STORE_BF16)
+        out = torch.mm(x2, w.t(), out_dtype=torch.float32) if out_f32 else torch.mm(x2, w.t())
         ctx.save_for_backward(x2, w)
         ctx.shape = x.shape
         return out.view(*x.shape[:-1], w.shape[0])
@@ -72,11 +82,8 @@ class Linear(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w = ctx.saved_tensors
         g = _flat(dy).to(torch.bfloat16)
-        dx = torch.empty_like(x2)
-        gemm(g, False, w, True, dx, STORE_BF16)
-        dw = torch.empty(w.shape, device=w.device, dtype=torch.float32)
-        gemm(g, True, x2, True, dw, STORE_F32)
-        return dx.view(ctx.shape), dw, None
+        dx = g @ w
+        return dx.view(ctx.shape), weight_grad(g, x2), None
 
 
 class LinearResidual(torch.autograd.Function):
@@ -100,10 +107,8 @@ class LinearResidual(torch.autograd.Function):
         x2, w = ctx.saved_tensors
         d32 = _flat(dout)
         g = d32.to(torch.bfloat16)
-        dx = torch.empty_like(x2)
-        gemm(g, False, w, True, dx, STORE_BF16)
-        dw = torch.empty(w.shape, device=w.device, dtype=torch.float32)
-        gemm(g, True, x2, True, dw, STORE_F32)
+        dx = g @ w
+        dw = weight_grad(g, x2)
         db = d32.sum(0) if ctx.has_bias else None
         return dx.view(ctx.shape), dw, db, dout
 
@@ -133,16 +138,13 @@ class FFNResidual(torch.autograd.Function):
         d32 = _flat(dout)
         g = d32.to(torch.bfloat16)
         db2 = d32.sum(0)
-        dw2 = torch.empty(w2b.shape, device=g.device, dtype=torch.float32)
-        gemm(g, True, u, True, dw2, STORE_F32)
+        dw2 = weight_grad(g, u)
         dh_pre = torch.empty_like(pre)
         partial = torch.empty(-(-g.shape[0] // TILE_M), pre.shape[1], device=g.device, dtype=torch.float32)
         gemm(g, False, w2b, True, dh_pre, GELU_BACK, aux=pre, partial=partial)
         db1 = partial.sum(0)
-        dw1 = torch.empty(w1b.shape, device=g.device, dtype=torch.float32)
-        gemm(dh_pre, True, h2, True, dw1, STORE_F32)
-        dh = torch.empty_like(h2)
-        gemm(dh_pre, False, w1b, True, dh, STORE_BF16)
+        dw1 = weight_grad(dh_pre, h2)
+        dh = dh_pre @ w1b
         return dh.view(ctx.shape), dout, dw1, db1, dw2, db2
 
 

@@ -82,7 +82,8 @@ def test_gated_tc_many_query_tiles(b, d):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("n,b,d,prev", [(37, 16, 64, False), (64, 16, 64, True), (100, 32, 32, True),
-                                        (5, 8, 16, False), (130, 16, 128, True)])
+                                        (5, 8, 16, False), (130, 16, 128, True), (300, 16, 64, True),
+                                        (1000, 16, 64, False), (129, 16, 64, True)])
 def test_local_attention_matches_reference(n, b, d, prev, dtype):
     torch.manual_seed(3)
     heads, start = 3, 4 * b
