@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--config", default=str(CONFIG))
     p.add_argument("--cp", type=int, default=0, help="context parallel size (default: all ranks)")
     p.add_argument("--recompute", action="store_true", help="activation recomputation (same on both arms)")
+    p.add_argument("--cuda-graph", dest="cuda_graph", action=argparse.BooleanOptionalAction, default=True,
+                   help="our arm: replay each training step from a CUDA graph")
     return p.parse_args()
 
 
@@ -140,22 +142,35 @@ def run_ours(args, rank, world, local_rank):
                                 loss_chunk=targs.loss_chunk)
     model = build_model({"model": "stack", **options}, execution=execution, device=device)
     model.train()
-    trainer = Trainer(targs, model, parallel)
+    fused_exchange = parallel.attach_fused(device)
+    graphed = args.cuda_graph
+    if graphed:
+        from exploration_b200.runtime.engine import lr_factor
+        from exploration_b200.runtime.flat import GraphTrainer
+        trainer = GraphTrainer(targs, model, parallel)
+    else:
+        trainer = Trainer(targs, model, parallel)
     ext = _native.load()
     generator = torch.Generator().manual_seed(100 + parallel.dp_rank)
     h2d = d2h = 0
 
     def step(index):
         nonlocal h2d, d2h
+        ids, target, mask, _ = make_batch(targs, generator)
+        shard = -(-ids.shape[1] // (model.block_size * cp)) * model.block_size
+        h2d = shard * ids.shape[0] * (ids.element_size() + target.element_size() + mask.element_size())
+        if graphed:
+            # Pinned inputs are copied to the device and the statistics back to
+            # pinned memory inside the replayed graph; reading them is the D2H.
+            stats, _ = trainer.step(ids, target, mask, targs.lr * lr_factor(index, targs.steps))
+            d2h = 6 * 8
+            return float(stats[0])
         trainer.optimizer.zero_grad(set_to_none=True)
         trainer.set_lr(index)
-        ids, target, mask, _ = make_batch(targs, generator)
         ids, target, mask = ids.pin_memory(), target.pin_memory(), mask.pin_memory()
         stats = trainer.micro_step(ids, target, mask, last=True)
         trainer.finish_step()
         loss = float(stats[0])                     # device -> host read of the step's result
-        shard = -(-ids.shape[1] // (model.block_size * cp)) * model.block_size
-        h2d = shard * ids.shape[0] * (ids.element_size() + target.element_size() + mask.element_size())
         d2h = stats.element_size() * stats.numel()
         return loss
 
@@ -179,6 +194,8 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         wall = time.perf_counter() - wall0
     launches = ext.launch_count() - launches0
+    if graphed:
+        launches += trainer.graph_launches * args.steps          # kernels replayed from the graph
     elapsed = torch.tensor([start.elapsed_time(end) / 1e3, wall], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
@@ -196,13 +213,18 @@ def run_ours(args, rank, world, local_rank):
             "config": {"model": "stack_100m", "global_batch": parallel.dp_size, "seq_len": args.length,
                        "parallelism": f"cp{cp}" + (f"xdp{parallel.dp_size}" if parallel.dp_size > 1 else ""),
                        "activation_recompute": bool(args.recompute), "optimizer": "fused AdamW fp32 master",
-                       "l2": "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)"},
+                       "l2": "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)",
+                       "ulysses_exchange": "nvlink-fused" if fused_exchange else ("nccl" if cp > 1 else "none"),
+                       "cuda_graph": bool(graphed), "optimizer_shard": bool(targs.optimizer_shard)},
             "clocks": sampler.summary(),
             "e2e": {"value": round(tokens / wall_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "gpu_launches": int(launches),
             "final_loss": round(losses[-1] / max(1, args.length // cp), 4),
         }
+    if graphed:
+        trainer.close()
+    parallel.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

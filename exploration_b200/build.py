@@ -25,6 +25,7 @@ SOURCES = [
     "bindings.cpp",
     "fused/norm_act.cu",
     "fused/loss_optim.cu",
+    "fused/flat_optim.cu",
     "attention/local_halo.cu",
     "attention/local_halo_b16.cu",
     "attention/gated_entry.cu",
@@ -33,6 +34,7 @@ SOURCES = [
     "attention/gated_tc_bwd.cu",
     "sparse/sparse_read.cu",
     "gemm/gemm_tc.cu",
+    "comm/symm_heap.cu",
 ]
 
 CUDA_FLAGS = [

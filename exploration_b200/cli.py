@@ -61,6 +61,9 @@ OPTIONS = [
     ("--activation-offload", TRAIN, dict(action="store_true",
                                          help="offload autograd saved tensors to pinned host RAM")),
     ("--optimizer-shard", TRAIN, dict(action=BOOL, default=True)),
+    ("--cuda-graph", TRAIN, dict(dest="cuda_graph", action=BOOL, default=False,
+                                 help="capture each training step in a CUDA graph (flat AdamW, "
+                                      "explicit gradient reduction; CUDA, one micro-step)")),
     ("--encoder-chunk", EXEC, dict(type=int, default=1024)),
     ("--query-chunk", EXEC, dict(type=int, default=0, help="queries per tile; 0 = automatic")),
     ("--loss-chunk", EXEC, dict(type=int, default=128)),

@@ -47,6 +47,28 @@ bool gemm_supported(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
           double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
           const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial);
+void gemm_scatter(const at::Tensor& a, const at::Tensor& b, bool b_mn, const std::vector<int64_t>& dst,
+                  int64_t rank, int64_t parts, int64_t batch, int64_t n_local, int64_t C);
+void gemm_gather(const std::vector<int64_t>& src, int64_t rank, int64_t parts, int64_t batch, int64_t n_local,
+                 int64_t C, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
+                 const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual);
+int64_t heap_alloc(int64_t bytes, int64_t device);
+void heap_free(int64_t ptr, int64_t device);
+at::Tensor heap_ipc_handle(int64_t ptr, int64_t device);
+int64_t heap_open(const at::Tensor& handle, int64_t device);
+void heap_close(int64_t ptr, int64_t device);
+at::Tensor heap_tensor(int64_t base, int64_t bytes_offset, at::IntArrayRef sizes, at::ScalarType dtype,
+                       int64_t device);
+int64_t heap_signal_bytes();
+void heap_barrier(const std::vector<int64_t>& bases, int64_t rank, double timeout_s);
+void gather_rows(const std::vector<int64_t>& src, int64_t rank, int64_t parts, int64_t batch, int64_t n_local,
+                 int64_t C, at::Tensor& out);
+void flat_sq_norm(const at::Tensor& grad, at::Tensor& hyper);
+void flat_adamw(at::Tensor& param, const at::Tensor& grad, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
+                const c10::optional<at::Tensor>& shadow, const at::Tensor& hyper,
+                const c10::optional<at::Tensor>& loss_check, double beta1, double beta2, double eps,
+                double decay);
+void flat_cast_bf16(const at::Tensor& x, at::Tensor& out);
 std::vector<at::Tensor> sparse_pop(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                    const at::Tensor& pos, const at::Tensor& ids, const at::Tensor& scores,
                                    const at::Tensor& log_zr, int64_t block, int64_t offset);
@@ -84,6 +106,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_pop", &eb::sparse_pop);
   m.def("gemm_supported", &eb::gemm_supported);
   m.def("gemm", &eb::gemm, "persistent tcgen05 GEMM with fused epilogues");
+  m.def("gemm_scatter", &eb::gemm_scatter, "projection GEMM whose epilogue stores head shards to their owners");
+  m.def("gemm_gather", &eb::gemm_gather, "GEMM whose A operand is read from the owners' head shards");
+  m.def("heap_alloc", &eb::heap_alloc);
+  m.def("heap_free", &eb::heap_free);
+  m.def("heap_ipc_handle", &eb::heap_ipc_handle);
+  m.def("heap_open", &eb::heap_open);
+  m.def("heap_close", &eb::heap_close);
+  m.def("heap_tensor", &eb::heap_tensor);
+  m.def("heap_signal_bytes", &eb::heap_signal_bytes);
+  m.def("heap_barrier", &eb::heap_barrier, "bounded all-rank barrier over peer signal words");
+  m.def("gather_rows", &eb::gather_rows, "sequence-layout copy of rank-sharded head buffers");
+  m.def("flat_sq_norm", &eb::flat_sq_norm, "hyper[3] = sum of squares of a flat fp32 buffer");
+  m.def("flat_adamw", &eb::flat_adamw, "AdamW over a flat buffer with device-side lr/step/clip");
+  m.def("flat_cast_bf16", &eb::flat_cast_bf16);
   m.def("launch_count", &eb::launch_count, "kernels launched by this extension so far");
   m.def("device_errors", &device_errors, "read and clear (site, cta) of the last bounded-wait timeout");
 }

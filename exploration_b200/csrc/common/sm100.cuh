@@ -1,5 +1,5 @@
 // sm_100a building blocks written as inline PTX: mbarriers with bounded
-// waits, TMA tiled loads (no multicast), TMEM allocation and tcgen05
+// waits, TMA tiled loads (each into the issuing CTA only), TMEM allocation and tcgen05
 // MMA / load / store / commit.
 //
 // Every wait is bounded. A wait that runs out sets a CTA-shared abort word
@@ -95,7 +95,7 @@ EB_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, Er
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled loads into the issuing CTA only)
 // ---------------------------------------------------------------------------
 
 EB_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
@@ -103,6 +103,14 @@ EB_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
       "%5}], [%6];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+EB_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -61,6 +61,25 @@ inline CUtensorMap make_matrix_map(const void* base, int64_t rows, int64_t cols,
   return map;
 }
 
+// bf16 tensor [planes, rows, cols] (cols contiguous, dense) with boxes of
+// 64 columns x box_rows rows x 1 plane, 128-byte swizzle. `base` may be a
+// peer GPU's memory mapped into this process (plain tiled loads only).
+inline CUtensorMap make_plane_map(const void* base, int64_t planes, int64_t rows, int64_t cols, int box_rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((cols * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2, static_cast<cuuint64_t>(rows) * cols * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult res = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", static_cast<int>(res));
+  return map;
+}
+
 // One error slot per device, allocated on first use and kept for the process
 // (defined in attention/gated_entry.cu).
 sm100::ErrorSlot* device_error_slot(int device);

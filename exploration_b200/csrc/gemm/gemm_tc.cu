@@ -14,10 +14,10 @@
 // output row) through the fused epilogue while the next tile accumulates.
 //
 // Epilogues: bf16 store | fp32 store | fp32 accumulate-into (weight grads) |
-// bias + exact GELU -> bf16 (pre-activation kept for backward) |
+// bias + exact GELU -> bf16 (gelu'(pre-activation) kept for backward) |
 // bias + fp32 residual -> fp32 (residual stream) |
-// GELU backward (acc * gelu'(pre)) -> bf16 with per-tile column sums for the
-// bias gradient.
+// GELU backward (acc * the kept gelu') -> bf16 with per-tile column sums for
+// the bias gradient | peer scatter (Ulysses to-heads).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -34,7 +34,7 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;   // warps 0-3: TMA, MMA, TMEM owner, idle; 4-11: epilogue
 constexpr int kGroupM = 8;
 
 enum Epilogue : int {
@@ -44,6 +44,23 @@ enum Epilogue : int {
   kBiasGeluBf16 = 3,
   kBiasResidualF32 = 4,
   kGeluBackBf16 = 5,
+  kScatterBf16 = 6,        // bf16 tile stored straight into the owning rank's buffer (Ulysses to-heads)
+};
+
+constexpr int kMaxPeers = 8;
+
+// Ulysses layout shared by the peer-scatter epilogue and the peer-gather A
+// operand. Every rank holds a buffer [parts, batch, n_total, C] for its C =
+// heads_per_rank * head_dim columns of each part (q; or k and v) over the
+// whole sequence; rank r's sequence shard is rows [r * n_local, (r+1) * n_local).
+// In the sequence layout a row has parts * dim columns, dim = world * C.
+struct PeerLayout {
+  int world, rank, parts, batch, n_local, n_total, C, dim;
+  __nv_bfloat16* dst[kMaxPeers];   // scatter targets (possibly peer memory)
+};
+
+struct PeerMaps {
+  CUtensorMap map[kMaxPeers];      // gather sources, one 3-D map per rank
 };
 
 struct GemmArgs {
@@ -53,11 +70,13 @@ struct GemmArgs {
   const float* bias;       // [N]
   const float* residual;   // fp32 [M, ldr]
   int64_t ldr;
-  __nv_bfloat16* aux;      // pre-activation (written by kBiasGeluBf16, read by kGeluBackBf16)
+  __nv_bfloat16* aux;      // gelu'(pre-activation) (written by kBiasGeluBf16, read by kGeluBackBf16)
   int64_t ld_aux;
   float* col_partial;      // [tiles_m, N] fp32 partial column sums (kGeluBackBf16)
   float alpha;
+  int vec;                 // 1: every row start and leading dimension allows 8/16-byte vector access
   ErrorSlot* err;
+  PeerLayout peer;
 };
 
 template <int BN>
@@ -67,12 +86,117 @@ struct alignas(1024) GemmSmem {
   uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
-  float colsum[4][BN];     // per-warp column partials of the GELU-backward epilogue
+  float4 stage[8][32 * 4]; // per epilogue warp: 32 rows x 16 fp32 columns, 16-byte units swizzled
+  float colsum[8][BN / 2]; // per epilogue warp column partials of the GELU-backward epilogue
 };
 
-EB_DEVICE float gelu_f(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
-EB_DEVICE float gelu_grad_f(float v) {
-  return 0.5f * (1.f + erff(v * 0.70710678118654752f)) + v * expf(-0.5f * v * v) * 0.39894228040143268f;
+// Exact GELU and its derivative from one erf: gelu(v) = v * Phi(v),
+// gelu'(v) = Phi(v) + v * phi(v) (Phi/phi: standard normal cdf/pdf).
+EB_DEVICE void gelu_and_grad(float v, float& y, float& dy) {
+  const float cdf = 0.5f * (1.f + erff(v * 0.70710678118654752f));
+  y = v * cdf;
+  dy = cdf + v * expf(-0.5f * v * v) * 0.39894228040143268f;
+}
+
+EB_DEVICE float4 load_bias4(const float* bias, int n, int N) {
+  if (n + 4 <= N && (reinterpret_cast<uintptr_t>(bias + n) & 15) == 0) return *reinterpret_cast<const float4*>(bias + n);
+  float b[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) b[t] = n + t < N ? bias[n + t] : 0.f;
+  return make_float4(b[0], b[1], b[2], b[3]);
+}
+
+// Four consecutive outputs (m, n..n+3) of one row. Vector accesses need the
+// row start aligned (checked on the host: GemmArgs::vec) and n + 4 <= N.
+template <int EPI>
+EB_DEVICE void epilogue4(const GemmArgs& g, int m, int n, float4 v4, float4 b4, float (&cs)[4]) {
+  float v[4] = {v4.x, v4.y, v4.z, v4.w};
+  const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+  const bool vec = g.vec && n + 4 <= g.N;
+  const int cnt = min(4, g.N - n);
+  if constexpr (EPI == kStoreBf16 || EPI == kBiasGeluBf16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(g.out) + static_cast<int64_t>(m) * g.ldo + n;
+    float pre[4];   // kBiasGeluBf16: gelu'(pre-activation), the backward's multiplier
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      if constexpr (EPI == kBiasGeluBf16) {
+        gelu_and_grad(v[t] + bb[t], v[t], pre[t]);
+      } else {
+        pre[t] = v[t];
+      }
+    }
+    if (vec) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+      if constexpr (EPI == kBiasGeluBf16)
+        *reinterpret_cast<uint2*>(g.aux + static_cast<int64_t>(m) * g.ld_aux + n) =
+            make_uint2(pack_bf16(pre[0], pre[1]), pack_bf16(pre[2], pre[3]));
+    } else {
+      for (int t = 0; t < cnt; ++t) {
+        o[t] = __float2bfloat16(v[t]);
+        if constexpr (EPI == kBiasGeluBf16) g.aux[static_cast<int64_t>(m) * g.ld_aux + n + t] = __float2bfloat16(pre[t]);
+      }
+    }
+  } else if constexpr (EPI == kStoreF32 || EPI == kAccumF32 || EPI == kBiasResidualF32) {
+    float* o = static_cast<float*>(g.out) + static_cast<int64_t>(m) * g.ldo + n;
+    const float* res = EPI == kBiasResidualF32 ? g.residual + static_cast<int64_t>(m) * g.ldr + n : nullptr;
+    if (vec) {
+      if constexpr (EPI == kAccumF32) {
+        const float4 p = *reinterpret_cast<const float4*>(o);
+        v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+      } else if constexpr (EPI == kBiasResidualF32) {
+        const float4 p = *reinterpret_cast<const float4*>(res);
+        v[0] += p.x + bb[0]; v[1] += p.y + bb[1]; v[2] += p.z + bb[2]; v[3] += p.w + bb[3];
+      }
+      *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      for (int t = 0; t < cnt; ++t) {
+        float val = v[t];
+        if constexpr (EPI == kAccumF32) val += o[t];
+        if constexpr (EPI == kBiasResidualF32) val += res[t] + bb[t];
+        o[t] = val;
+      }
+    }
+  } else if constexpr (EPI == kScatterBf16) {
+    // Sequence-layout element (m, n) -> owner's head-layout buffer.
+    const PeerLayout& L = g.peer;
+    const int b = m / L.n_local, t = m - b * L.n_local;
+    const int part = n / L.dim, within = n - part * L.dim;
+    const int owner = within / L.C, c = within - owner * L.C;
+    __nv_bfloat16* o = L.dst[owner] +
+                       (static_cast<int64_t>(part * L.batch + b) * L.n_total + L.rank * L.n_local + t) * L.C + c;
+    if (vec && c + 4 <= L.C) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+    } else {
+      for (int q = 0; q < cnt; ++q) {
+        const int nn = n + q, pp = nn / L.dim, ww = nn - pp * L.dim, ow = ww / L.C, cc = ww - ow * L.C;
+        L.dst[ow][(static_cast<int64_t>(pp * L.batch + b) * L.n_total + L.rank * L.n_local + t) * L.C + cc] =
+            __float2bfloat16(v[q]);
+      }
+    }
+  } else if constexpr (EPI == kGeluBackBf16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(g.out) + static_cast<int64_t>(m) * g.ldo + n;
+    const __nv_bfloat16* a = g.aux + static_cast<int64_t>(m) * g.ld_aux + n;
+    float pre[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(a);
+      const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+      const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+      pre[0] = __low2float(p0); pre[1] = __high2float(p0); pre[2] = __low2float(p1); pre[3] = __high2float(p1);
+    } else {
+      for (int t = 0; t < cnt; ++t) pre[t] = __bfloat162float(a[t]);
+    }
+    float d[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      d[t] = t < cnt ? v[t] * pre[t] : 0.f;
+      cs[t] += d[t];
+    }
+    if (vec) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16(d[0], d[1]), pack_bf16(d[2], d[3]));
+    } else {
+      for (int t = 0; t < cnt; ++t) o[t] = __float2bfloat16(d[t]);
+    }
+  }
 }
 
 EB_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -85,9 +209,10 @@ EB_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn)
   tn = in_group / rows;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, GemmArgs g) {
+gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, GemmArgs g,
+               const __grid_constant__ PeerMaps pm) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
   GemmSmem<BN>& sm = *reinterpret_cast<GemmSmem<BN>*>(
       (reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -105,7 +230,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 128);
+      mbar_init(&sm.acc_empty[s], 256);
     }
     sm.abort = 0;
     fence_barrier_init();
@@ -118,7 +243,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 
   if (warp == 0) {
     if (lane == 0) {
-      prefetch_tensormap(&ta);
+      if constexpr (GATHER_A) {
+        for (int r = 0; r < g.peer.world; ++r) prefetch_tensormap(&pm.map[r]);
+      } else {
+        prefetch_tensormap(&ta);
+      }
       prefetch_tensormap(&tb);
       int it = 0;   // global k-slice counter across tiles
       bool ok = true;
@@ -133,7 +262,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
           }
           mbar_expect_tx(&sm.full[s], kStageBytes);
           const int k0 = kb * kBK;
-          if constexpr (A_MN) {   // A stored [K, M]: boxes of 64 m x 64 k
+          if constexpr (GATHER_A) {
+            // A = the sequence layout of rank-sharded head buffers: the 64-wide
+            // k-slice lives on one owner; rows are this rank's shard.
+            const PeerLayout& L = g.peer;
+            const int m0 = tm * kBM, b = m0 / L.n_local, t0 = m0 - b * L.n_local;
+            const int part = k0 / L.dim, within = k0 - part * L.dim;
+            const int owner = within / L.C, col = within - owner * L.C;
+            tma_load_3d(sm.a[s], &pm.map[owner], &sm.full[s], col, L.rank * L.n_local + t0, part * L.batch + b);
+          } else if constexpr (A_MN) {   // A stored [K, M]: boxes of 64 m x 64 k
             tma_load_2d(sm.a[s], &ta, &sm.full[s], tm * kBM, k0);
             tma_load_2d(sm.a[s] + 64 * kBK, &ta, &sm.full[s], tm * kBM + 64, k0);
           } else {                // A stored [M, K]: one box of 64 k x 128 m
@@ -181,9 +318,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       }
     }
   } else if (warp >= 4) {
-    const int ew = warp - 4;
-    const int row = threadIdx.x - 128;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(ew * 32) << 16);
+    // Two epilogue warpgroups split the tile's columns. Each warp owns 32
+    // accumulator lanes (rows); a row's values go through a small swizzled
+    // shared-memory stage so that global loads/stores are coalesced (four
+    // lanes cover 16 consecutive columns of one row).
+    const int ew = warp - 4;                  // 0..7
+    const int grp = ew >> 2;                  // column half of the tile
+    const int wr = ew & 3;                    // TMEM lane quarter (rows 32*wr..)
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(wr * 32) << 16);
+    float4* stage = sm.stage[ew];
+    const int rq = lane >> 2, u = lane & 3;
     int local = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
       int tm, tn;
@@ -192,121 +336,66 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       const bool ready = mbar_wait(&sm.acc_full[acc], (local >> 1) & 1, abort, g.err, kSiteGemm);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      const int m = tm * kBM + row;
-      const bool row_ok = m < g.M;
-      if constexpr (EPI == kGeluBackBf16) {
-        for (int c = lane; c < BN; c += 32) sm.colsum[ew][c] = 0.f;
-        __syncwarp();
-      }
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = grp * (BN / 2); c0 < (grp + 1) * (BN / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + acc * BN + c0, r);
         tc_wait_ld();
-        const int n0 = tn * BN + c0;
-        float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * g.alpha;
-        const bool full_chunk = n0 + 32 <= g.N;
-        if constexpr (EPI == kStoreBf16 || EPI == kBiasGeluBf16) {
-          __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(g.out) + static_cast<int64_t>(m) * g.ldo + n0;
-          __nv_bfloat16* arow = EPI == kBiasGeluBf16 ? g.aux + static_cast<int64_t>(m) * g.ld_aux + n0 : nullptr;
+        for (int half = 0; half < 2; ++half) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float pre[8], post[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              pre[t] = v[i + t];
-              if constexpr (EPI == kBiasGeluBf16) {
-                const int n = n0 + i + t;
-                pre[t] += n < g.N ? g.bias[n] : 0.f;
-                post[t] = gelu_f(pre[t]);
-              } else {
-                post[t] = pre[t];
-              }
-            }
-            if (row_ok && full_chunk) {
-              *reinterpret_cast<uint4*>(orow + i) = make_uint4(pack_bf16(post[0], post[1]), pack_bf16(post[2], post[3]),
-                                                               pack_bf16(post[4], post[5]), pack_bf16(post[6], post[7]));
-              if constexpr (EPI == kBiasGeluBf16)
-                *reinterpret_cast<uint4*>(arow + i) = make_uint4(pack_bf16(pre[0], pre[1]), pack_bf16(pre[2], pre[3]),
-                                                                 pack_bf16(pre[4], pre[5]), pack_bf16(pre[6], pre[7]));
-            } else if (row_ok) {
-#pragma unroll
-              for (int t = 0; t < 8; ++t) {
-                if (n0 + i + t < g.N) {
-                  orow[i + t] = __float2bfloat16(post[t]);
-                  if constexpr (EPI == kBiasGeluBf16) arow[i + t] = __float2bfloat16(pre[t]);
-                }
-              }
-            }
+          for (int q = 0; q < 4; ++q) {
+            const int j = half * 16 + 4 * q;
+            stage[lane * 4 + (q ^ ((lane >> 1) & 3))] =
+                make_float4(__uint_as_float(r[j]) * g.alpha, __uint_as_float(r[j + 1]) * g.alpha,
+                            __uint_as_float(r[j + 2]) * g.alpha, __uint_as_float(r[j + 3]) * g.alpha);
           }
-        } else if constexpr (EPI == kStoreF32 || EPI == kAccumF32 || EPI == kBiasResidualF32) {
-          float* orow = static_cast<float*>(g.out) + static_cast<int64_t>(m) * g.ldo + n0;
-          const float* rrow = EPI == kBiasResidualF32 ? g.residual + static_cast<int64_t>(m) * g.ldr + n0 : nullptr;
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            float o[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) o[t] = v[i + t];
-            if (row_ok && full_chunk) {
-              if constexpr (EPI == kAccumF32) {
-                const float4 prev = *reinterpret_cast<const float4*>(orow + i);
-                o[0] += prev.x; o[1] += prev.y; o[2] += prev.z; o[3] += prev.w;
-              } else if constexpr (EPI == kBiasResidualF32) {
-                const float4 res = *reinterpret_cast<const float4*>(rrow + i);
-                o[0] += res.x + (g.bias ? g.bias[n0 + i] : 0.f);
-                o[1] += res.y + (g.bias ? g.bias[n0 + i + 1] : 0.f);
-                o[2] += res.z + (g.bias ? g.bias[n0 + i + 2] : 0.f);
-                o[3] += res.w + (g.bias ? g.bias[n0 + i + 3] : 0.f);
-              }
-              *reinterpret_cast<float4*>(orow + i) = make_float4(o[0], o[1], o[2], o[3]);
-            } else if (row_ok) {
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const int n = n0 + i + t;
-                if (n < g.N) {
-                  float val = o[t];
-                  if constexpr (EPI == kAccumF32) val += orow[i + t];
-                  if constexpr (EPI == kBiasResidualF32) val += rrow[i + t] + (g.bias ? g.bias[n] : 0.f);
-                  orow[i + t] = val;
-                }
-              }
-            }
+          __syncwarp();
+          const int n = tn * BN + c0 + half * 16 + 4 * u;
+          float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if constexpr (EPI == kBiasGeluBf16 || EPI == kBiasResidualF32) {
+            if (g.bias) bias4 = load_bias4(g.bias, n, g.N);
           }
-        } else if constexpr (EPI == kGeluBackBf16) {
-          __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(g.out) + static_cast<int64_t>(m) * g.ldo + n0;
-          const __nv_bfloat16* arow = g.aux + static_cast<int64_t>(m) * g.ld_aux + n0;
+          float cs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int n = n0 + i;
-            float d = 0.f;
-            if (row_ok && n < g.N) {
-              d = v[i] * gelu_grad_f(__bfloat162float(arow[i]));
-              orow[i] = __float2bfloat16(d);
+          for (int it = 0; it < 4; ++it) {
+            const int rr = it * 8 + rq;
+            const float4 v = stage[rr * 4 + (u ^ ((rr >> 1) & 3))];
+            const int m = tm * kBM + wr * 32 + rr;
+            if (m < g.M && n < g.N) epilogue4<EPI>(g, m, n, v, bias4, cs);
+          }
+          __syncwarp();
+          if constexpr (EPI == kGeluBackBf16) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+#pragma unroll
+              for (int o = 4; o < 32; o <<= 1) cs[t] += __shfl_xor_sync(0xffffffffu, cs[t], o);
             }
-            // Column partial sums over this warp's 32 rows (deterministic tree).
-            float s = d;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0) sm.colsum[ew][c0 + i] = s;
+            if (lane < 4) {
+              float* dst = &sm.colsum[ew][c0 - grp * (BN / 2) + half * 16 + 4 * u];
+              dst[0] = cs[0]; dst[1] = cs[1]; dst[2] = cs[2]; dst[3] = cs[3];
+            }
           }
         }
       }
       if constexpr (EPI == kGeluBackBf16) {
-        // Combine the four warps' partials of this tile; one row per tile of output.
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        for (int c = row; c < BN; c += 128) {
-          const int n = tn * BN + c;
+        // Combine the group's four row-quarters; one partial row per output tile.
+        const int gt = threadIdx.x - 128 - grp * 128;
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
+        for (int c = gt; c < BN / 2; c += 128) {
+          const int n = tn * BN + grp * (BN / 2) + c;
           if (n < g.N)
-            g.col_partial[static_cast<int64_t>(tm) * g.N + n] =
-                sm.colsum[0][c] + sm.colsum[1][c] + sm.colsum[2][c] + sm.colsum[3][c];
+            g.col_partial[static_cast<int64_t>(tm) * g.N + n] = sm.colsum[grp * 4][c] + sm.colsum[grp * 4 + 1][c] +
+                                                               sm.colsum[grp * 4 + 2][c] + sm.colsum[grp * 4 + 3][c];
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
       }
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[acc]);
     }
+    // Peer stores complete at system scope before the kernel ends, so a
+    // barrier issued after it publishes them.
+    if constexpr (EPI == kScatterBf16) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();
@@ -316,36 +405,40 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   }
 }
 
-// Operand descriptor: row-major storage [rows, cols] with a leading dimension.
-struct Operand {
-  const at::Tensor* t;
-  bool mn_major;   // true: stored [K, M or N]; false: stored [M or N, K]
-};
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A>
+void launch_gemm(const CUtensorMap& ta, const PeerMaps& pm, const at::Tensor& b, int M, int N, int K,
+                 GemmArgs& args, cudaStream_t stream) {
+  CUtensorMap tb = B_MN ? make_matrix_map(b.data_ptr(), K, N, b.stride(0), kBK)   // [K, N], box 64n x 64k
+                        : make_matrix_map(b.data_ptr(), N, K, b.stride(0), BN);   // [N, K], box 64k x BN n
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  int sms = 0;
+  EB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b.device().index()));
+  const int grid = std::min(tiles, sms);
+  const size_t smem = sizeof(GemmSmem<BN>) + 1024;
+  auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, EPI, GATHER_A>;
+  EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  kernel<<<grid, kThreads, smem, stream>>>(ta, tb, args, pm);
+}
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 void run_gemm(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args, cudaStream_t stream) {
   // TMA maps: inner (contiguous) dimension first.
   CUtensorMap ta = A_MN ? make_matrix_map(a.data_ptr(), K, M, a.stride(0), kBK)     // [K, M], box 64m x 64k
                         : make_matrix_map(a.data_ptr(), M, K, a.stride(0), kBM);    // [M, K], box 64k x 128m
-  CUtensorMap tb = B_MN ? make_matrix_map(b.data_ptr(), K, N, b.stride(0), kBK)
-                        : make_matrix_map(b.data_ptr(), N, K, b.stride(0), BN);
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  int sms = 0;
-  EB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, a.device().index()));
-  const int grid = std::min(tiles, sms);
-  const size_t smem = sizeof(GemmSmem<BN>) + 1024;
-  auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
-  EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kernel<<<grid, kThreads, smem, stream>>>(ta, tb, args);
+  PeerMaps none{};
+  launch_gemm<BN, A_MN, B_MN, EPI, false>(ta, none, b, M, N, K, args, stream);
+}
+
+bool wide_tiles(int M, int N) {
+  // Wide tiles when there is enough work to fill the GPU; narrow ones otherwise.
+  const long tiles256 = ((M + kBM - 1) / kBM) * static_cast<long>((N + 255) / 256);
+  return N >= 256 && tiles256 >= 148;
 }
 
 template <bool A_MN, bool B_MN, int EPI>
 void dispatch_bn(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args,
                  cudaStream_t stream) {
-  // Wide tiles when there is enough work to fill the GPU; narrow ones otherwise.
-  const int sms = 148;
-  const long tiles256 = ((M + kBM - 1) / kBM) * static_cast<long>((N + 255) / 256);
-  if (N >= 256 && tiles256 >= sms) run_gemm<256, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
+  if (wide_tiles(M, N)) run_gemm<256, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
   else run_gemm<128, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
 }
 
@@ -399,6 +492,14 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
   }
   if (col_partial.has_value() && col_partial->defined()) args.col_partial = col_partial->data_ptr<float>();
   args.err = device_error_slot(a.device().index());
+  {
+    // Vector epilogue accesses: 4 elements per access at column multiples of 4.
+    auto ok = [](const void* p, int64_t ld, int elem) {
+      return p == nullptr || ((reinterpret_cast<uintptr_t>(p) % 16) == 0 && (ld * elem) % 16 == 0);
+    };
+    args.vec = ok(args.out, args.ldo, out.element_size()) && ok(args.residual, args.ldr, 4) &&
+               ok(args.aux, args.ld_aux, 2);
+  }
   auto stream = at::cuda::getCurrentCUDAStream();
   switch (epilogue) {
     case kStoreBf16:
@@ -421,6 +522,132 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
       dispatch_layout<kGeluBackBf16>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
     default:
       TORCH_CHECK(false, "unknown epilogue ", epilogue);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(1);
+}
+
+namespace {
+
+PeerLayout make_layout(int64_t world, int64_t rank, int64_t parts, int64_t batch, int64_t n_local, int64_t C) {
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "ulysses gemm: bad world/rank");
+  TORCH_CHECK(parts >= 1 && batch >= 1 && n_local >= 1 && C >= 1, "ulysses gemm: bad layout");
+  PeerLayout L{};
+  L.world = static_cast<int>(world);
+  L.rank = static_cast<int>(rank);
+  L.parts = static_cast<int>(parts);
+  L.batch = static_cast<int>(batch);
+  L.n_local = static_cast<int>(n_local);
+  L.n_total = static_cast<int>(n_local * world);
+  L.C = static_cast<int>(C);
+  L.dim = static_cast<int>(world * C);
+  return L;
+}
+
+GemmArgs base_args(int M, int N, int K, const at::Tensor& ref) {
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.alpha = 1.f;
+  args.err = device_error_slot(ref.device().index());
+  return args;
+}
+
+}  // namespace
+
+// Ulysses to-heads fused with its projection: Y = A op(B)^T in the sequence
+// layout [batch * n_local, parts * world * C] is never materialised; each
+// 4-column group goes to `dst[owner]`, the owner's [parts, batch, n_total, C]
+// buffer (peer memory). Caller synchronises ranks afterwards.
+void gemm_scatter(const at::Tensor& a, const at::Tensor& b, bool b_mn, const std::vector<int64_t>& dst,
+                  int64_t rank, int64_t parts, int64_t batch, int64_t n_local, int64_t C) {
+  TORCH_CHECK(gemm_supported(a, false, b, b_mn), "gemm_scatter: bf16 2-D operands with 16-byte aligned rows");
+  const int64_t world = static_cast<int64_t>(dst.size());
+  PeerLayout L = make_layout(world, rank, parts, batch, n_local, C);
+  const int M = a.size(0), K = a.size(1);
+  const int N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK(M == batch * n_local && N == parts * world * C, "gemm_scatter: shapes do not match the layout");
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm_scatter: inner dimensions differ");
+  for (int r = 0; r < world; ++r) {
+    TORCH_CHECK(dst[r] % 16 == 0, "gemm_scatter: destination must be 16-byte aligned");
+    L.dst[r] = reinterpret_cast<__nv_bfloat16*>(dst[r]);
+  }
+  const c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args = base_args(M, N, K, a);
+  args.vec = (C % 4) == 0;
+  args.peer = L;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (b_mn) {
+    if (wide_tiles(M, N)) run_gemm<256, false, true, kScatterBf16>(a, b, M, N, K, args, stream);
+    else run_gemm<128, false, true, kScatterBf16>(a, b, M, N, K, args, stream);
+  } else {
+    if (wide_tiles(M, N)) run_gemm<256, false, false, kScatterBf16>(a, b, M, N, K, args, stream);
+    else run_gemm<128, false, false, kScatterBf16>(a, b, M, N, K, args, stream);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(1);
+}
+
+namespace {
+template <int EPI>
+void gather_dispatch(const PeerMaps& pm, const at::Tensor& b, bool b_mn, int M, int N, int K, GemmArgs& args,
+                     cudaStream_t stream) {
+  CUtensorMap none{};
+  const bool wide = wide_tiles(M, N);
+  if (b_mn) {
+    if (wide) launch_gemm<256, false, true, EPI, true>(none, pm, b, M, N, K, args, stream);
+    else launch_gemm<128, false, true, EPI, true>(none, pm, b, M, N, K, args, stream);
+  } else {
+    if (wide) launch_gemm<256, false, false, EPI, true>(none, pm, b, M, N, K, args, stream);
+    else launch_gemm<128, false, false, EPI, true>(none, pm, b, M, N, K, args, stream);
+  }
+}
+}  // namespace
+
+// Ulysses to-sequence fused with the next projection: A[m, k] is read tile
+// by tile with TMA straight from the owners' [parts, batch, n_total, C]
+// buffers (`src[r]`, peer memory; plain tiled loads), out = epilogue(A op(B)^T).
+void gemm_gather(const std::vector<int64_t>& src, int64_t rank, int64_t parts, int64_t batch, int64_t n_local,
+                 int64_t C, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
+                 const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual) {
+  const int64_t world = static_cast<int64_t>(src.size());
+  PeerLayout L = make_layout(world, rank, parts, batch, n_local, C);
+  TORCH_CHECK(C % 64 == 0, "gemm_gather: heads_per_rank * head_dim must be a multiple of 64");
+  TORCH_CHECK(n_local % kBM == 0, "gemm_gather: the local shard must be a multiple of 128 rows");
+  TORCH_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.dim() == 2 && aligned16(b), "gemm_gather: B");
+  const int M = batch * n_local, K = parts * world * C;
+  const int N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm_gather: inner dimensions differ");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "gemm_gather: bad output");
+  const c10::cuda::CUDAGuard guard(b.device());
+  PeerMaps pm{};
+  for (int r = 0; r < world; ++r)
+    pm.map[r] = make_plane_map(reinterpret_cast<const void*>(src[r]), parts * batch, L.n_total, C, kBM);
+  GemmArgs args = base_args(M, N, K, b);
+  args.peer = L;
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  args.bias = bias.has_value() && bias->defined() ? bias->data_ptr<float>() : nullptr;
+  if (residual.has_value() && residual->defined()) {
+    TORCH_CHECK(residual->scalar_type() == at::kFloat && residual->stride(1) == 1, "gemm_gather: fp32 residual");
+    args.residual = residual->data_ptr<float>();
+    args.ldr = residual->stride(0);
+  }
+  auto ok = [](const void* p, int64_t ld, int elem) {
+    return p == nullptr || ((reinterpret_cast<uintptr_t>(p) % 16) == 0 && (ld * elem) % 16 == 0);
+  };
+  args.vec = ok(args.out, args.ldo, out.element_size()) && ok(args.residual, args.ldr, 4);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  switch (epilogue) {
+    case kStoreBf16:
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16, "bf16 output");
+      gather_dispatch<kStoreBf16>(pm, b, b_mn, M, N, K, args, stream); break;
+    case kBiasResidualF32:
+      TORCH_CHECK(out.scalar_type() == at::kFloat && args.residual, "fp32 residual needed");
+      gather_dispatch<kBiasResidualF32>(pm, b, b_mn, M, N, K, args, stream); break;
+    default:
+      TORCH_CHECK(false, "gemm_gather: epilogue ", epilogue, " is not instantiated");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(1);

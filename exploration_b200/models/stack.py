@@ -164,6 +164,14 @@ class StackModel(nn.Module):
         for layer in self.local:
             halo = parallel.halo(x, self.block_size)
             x = layer(x, previous=halo, start=offset)
+        fused_exchange = None
+        if parallel.ulysses is not None and self._native(x):
+            h = fused.layer_norm(x, self.raw_kv.norm, self.backend)
+            fused_exchange = parallel.fused(h, self.heads, self.hd)
+        if fused_exchange is not None:
+            # K/V projection whose epilogue stores head shards to their owners.
+            kv = fused_exchange.project_to_heads(h, self.raw_kv.proj.weight, 2, self.heads, self.hd)
+            return x, kv[0], kv[1]
         raw_k, raw_v = self.raw_kv(x, None)
         return x, parallel.to_heads(raw_k), parallel.to_heads(raw_v)
 
@@ -190,6 +198,20 @@ class StackModel(nn.Module):
 
     def _dense_round(self, rd, z, k, v, positions, parallel):
         recompute = self.checkpoint_chunks and torch.is_grad_enabled()
+        if not recompute and parallel.ulysses is not None and self._native(z):
+            h = fused.layer_norm(z, rd.q_norm, self.backend)
+            fused_exchange = parallel.fused(h, self.heads, self.hd)
+            if fused_exchange is not None:
+                # Query projection -> head owners, attention, then the output
+                # projection reading the context straight from its owners.
+                q = fused_exchange.project_to_heads(h, rd.wq.weight, 1, self.heads, self.hd)[0]
+                if k.dtype != q.dtype:
+                    k, v = k.to(q.dtype), v.to(q.dtype)
+                ctx = dense_attention(q, k, v, positions, self.block_size, self.backend,
+                                      q_chunk=self.attention_q_chunk, kv_chunk=self.attention_kv_chunk)
+                z = fused_exchange.heads_to_linear_residual(ctx, rd.read_out, z)
+                return fused.ffn_residual(fused.layer_norm(z, rd.ffn_norm, self.backend), z, rd.ffn,
+                                          self.backend)
         if recompute:
             q = checkpoint(self._query, rd, z, use_reentrant=False, preserve_rng_state=False)
         else:
@@ -209,13 +231,18 @@ class StackModel(nn.Module):
         logits = fused.linear(h, self.lm_head, self.backend, out_f32=True)
         return fused.cross_entropy_sum(logits, labels, self.backend)
 
-    def forward_loss(self, input_ids, targets, sup=None, parallel=None, offset=0):
+    def forward_loss(self, input_ids, targets, sup=None, parallel=None, offset=0, static_width=False):
         """Dense training loss: returns sums and counts, never ``[B,N,V]``.
 
         Inputs are the local sequence shard under context parallelism. Every
         CP rank runs the same collectives, also when it owns no supervised
         token; the caller normalises by the global count
         (reference: st/models/stack.py:215-279).
+
+        ``static_width``: read every position of the shard (unsupervised ones
+        get position -1 and no loss) instead of compacting the supervised ones
+        first. The work no longer depends on the data and there is no host
+        synchronisation, which a captured CUDA graph needs; values are the same.
         """
         parallel = parallel or ParallelContext()
         if input_ids.ndim != 2 or input_ids.shape != targets.shape or min(input_ids.shape) < 1:
@@ -227,19 +254,27 @@ class StackModel(nn.Module):
         if sup.shape != targets.shape or sup.dtype != torch.bool:
             raise ValueError("sup must be bool [B,N]")
         sup = sup & (targets != -100)
+        parallel.begin_step()
         batch, n = input_ids.shape
         device = input_ids.device
-        width = parallel.max_query_count(int(sup.sum(1).max()), device)
-        # Sort integer positions (supervised first, in order), never features.
-        order = torch.arange(n, device=device)[None].expand(batch, -1)
-        order = torch.where(sup, order, n).sort(1).values
-        if width > n:
-            order = F.pad(order, (0, width - n), value=n)
-        order = order[:, :width]
-        valid = order < n
-        safe = order.clamp_max(n - 1)
-        pos = torch.where(valid, order + offset, -1)
-        picked = targets.gather(1, safe).masked_fill(~valid, -100)
+        if static_width:
+            width = n
+            safe = torch.arange(n, device=device)[None].expand(batch, -1)
+            valid = sup
+            pos = torch.where(valid, safe + offset, -1)
+            picked = targets.masked_fill(~valid, -100)
+        else:
+            width = parallel.max_query_count(int(sup.sum(1).max()), device)
+            # Sort integer positions (supervised first, in order), never features.
+            order = torch.arange(n, device=device)[None].expand(batch, -1)
+            order = torch.where(sup, order, n).sort(1).values
+            if width > n:
+                order = F.pad(order, (0, width - n), value=n)
+            order = order[:, :width]
+            valid = order < n
+            safe = order.clamp_max(n - 1)
+            pos = torch.where(valid, order + offset, -1)
+            picked = targets.gather(1, safe).masked_fill(~valid, -100)
         x, k, v = self.encode_shard(input_ids, parallel, offset)
         rows = torch.arange(batch, device=device)[:, None]
         native = self._native(x)
@@ -248,7 +283,10 @@ class StackModel(nn.Module):
         losses, hits = [], []
         for lo in range(0, width, step):
             hi = min(lo + step, width)
-            all_rows = lo == 0 and hi == n and not bool((~valid).any()) if native else False
+            if static_width:
+                all_rows = lo == 0 and hi == n
+            else:
+                all_rows = lo == 0 and hi == n and not bool((~valid).any()) if native else False
             z = x if all_rows else x[rows, safe[:, lo:hi]]
             positions = parallel.gather_positions(pos[:, lo:hi])
             for rd in self.reads:

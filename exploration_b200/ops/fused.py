@@ -42,10 +42,24 @@ def use_native(x: torch.Tensor, backend: str, cdt: torch.dtype) -> bool:
 # id(param) -> (weak reference to param, {dtype: (param version, copy)}). Tensors
 # define elementwise ``==``, so they cannot be keys of a WeakKeyDictionary.
 _cast_cache: dict = {}
+_shadows: dict = {}
+
+
+def register_shadow(param: torch.Tensor, shadow: torch.Tensor) -> None:
+    """Use ``shadow`` (kept current by the optimizer) as ``param``'s low-precision copy."""
+    key = id(param)
+    _shadows[key] = (weakref.ref(param, lambda _ref, k=key: _shadows.pop(k, None)), shadow)
+
+
+def clear_shadows() -> None:
+    _shadows.clear()
 
 
 def _cached_copy(param: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     key = id(param)
+    shadow = _shadows.get(key)
+    if shadow is not None and shadow[0]() is param and shadow[1].dtype == dtype:
+        return shadow[1]
     entry = _cast_cache.get(key)
     if entry is None or entry[0]() is not param:
         entry = (weakref.ref(param, lambda _ref, k=key: _cast_cache.pop(k, None)), {})

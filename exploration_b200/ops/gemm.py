@@ -9,9 +9,10 @@ elementwise work inside the GEMM epilogues:
 * ``linear_residual``: ``out = residual + x W^T (+ b)`` in fp32 (the residual
   stream update), one kernel instead of GEMM + add;
 * ``ffn_residual``: ``out = y + W2 gelu(W1 h + b1) + b2``; the first GEMM
-  applies bias + exact GELU and keeps the pre-activation for backward, the
-  second adds bias and residual; backward fuses the GELU derivative (and the
-  per-tile bias-gradient partial sums) into the ``dU = dOut W2`` epilogue.
+  applies bias + exact GELU and keeps ``gelu'`` of the pre-activation (bf16)
+  for backward, the second adds bias and residual; backward multiplies by
+  the kept derivative (and forms the per-tile bias-gradient partial sums) in
+  the ``dU = dOut W2`` epilogue, so no erf is evaluated twice.
 
 Weights stay fp32 parameters (autograd accumulates their fp32 gradients);
 the GEMMs read a bf16 copy refreshed once per optimizer step.
@@ -122,26 +123,26 @@ class FFNResidual(torch.autograd.Function):
         y2 = y.reshape(-1, y.shape[-1]).contiguous()
         w1b, w2b = _bf16_weight(w1), _bf16_weight(w2)
         rows, hidden = h2.shape[0], w1b.shape[0]
-        pre = torch.empty(rows, hidden, device=h.device, dtype=torch.bfloat16)
-        u = torch.empty_like(pre)
-        gemm(h2, False, w1b, False, u, BIAS_GELU, bias=b1, aux=pre)
+        dgelu = torch.empty(rows, hidden, device=h.device, dtype=torch.bfloat16)
+        u = torch.empty_like(dgelu)
+        gemm(h2, False, w1b, False, u, BIAS_GELU, bias=b1, aux=dgelu)
         out = torch.empty(y2.shape, device=h.device, dtype=torch.float32)
         gemm(u, False, w2b, False, out, BIAS_RESIDUAL, bias=b2, residual=y2)
-        ctx.save_for_backward(h2, pre, u, w1b, w2b)
+        ctx.save_for_backward(h2, dgelu, u, w1b, w2b)
         ctx.shape = h.shape
         return out.view(y.shape)
 
     @staticmethod
     @torch.autograd.function.once_differentiable
     def backward(ctx, dout):
-        h2, pre, u, w1b, w2b = ctx.saved_tensors
+        h2, dgelu, u, w1b, w2b = ctx.saved_tensors
         d32 = _flat(dout)
         g = d32.to(torch.bfloat16)
         db2 = d32.sum(0)
         dw2 = weight_grad(g, u)
-        dh_pre = torch.empty_like(pre)
-        partial = torch.empty(-(-g.shape[0] // TILE_M), pre.shape[1], device=g.device, dtype=torch.float32)
-        gemm(g, False, w2b, True, dh_pre, GELU_BACK, aux=pre, partial=partial)
+        dh_pre = torch.empty_like(dgelu)
+        partial = torch.empty(-(-g.shape[0] // TILE_M), dgelu.shape[1], device=g.device, dtype=torch.float32)
+        gemm(g, False, w2b, True, dh_pre, GELU_BACK, aux=dgelu, partial=partial)
         db1 = partial.sum(0)
         dw1 = weight_grad(dh_pre, h2)
         dh = dh_pre @ w1b

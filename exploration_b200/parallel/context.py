@@ -156,6 +156,35 @@ class ParallelContext:
         return cls(world, rank, cp_size, rank % cp_size, world // cp_size, rank // cp_size,
                    cp_group, dp_group)
 
+    def attach_fused(self, device, nbytes: int = 0) -> bool:
+        """Attach the NVLink-fused Ulysses exchange (CUDA, CP > 1; collective).
+
+        Disabled with ``EB200_FUSED_ULYSSES=0`` (the NCCL path is then used).
+        """
+        if self.cp_size == 1 or self.ulysses is not None:
+            return self.ulysses is not None
+        if torch.device(device).type != "cuda" or os.environ.get("EB200_FUSED_ULYSSES", "1") == "0":
+            return False
+        from .ulysses import UlyssesFused
+        self.ulysses = UlyssesFused(self.cp_group, self.cp_rank, self.cp_size, device, nbytes)
+        return True
+
+    def begin_step(self) -> None:
+        """Start of a micro-step: recycle the fused exchange's buffers."""
+        if self.ulysses is not None:
+            self.ulysses.begin_step()
+
+    def fused(self, x, heads, head_dim):
+        """The fused exchange when it applies to ``x`` (same answer on every rank)."""
+        if self.ulysses is not None and self.ulysses.usable(x, heads, head_dim):
+            return self.ulysses
+        return None
+
+    def close(self) -> None:
+        if self.ulysses is not None:
+            self.ulysses.close()
+            self.ulysses = None
+
     def shard(self, tensor, block_size, value=0):
         """``[B, N, ...]`` -> this rank's equal, block-aligned slice (tail padded with ``value``)."""
         n = tensor.shape[1]

@@ -165,8 +165,20 @@ class Trainer:
         return norm
 
 
+def use_graph_trainer(args, model, device) -> bool:
+    """The CUDA-graph step applies to Stack models on CUDA with one micro-step and no offload."""
+    return (getattr(args, "cuda_graph", False) and device.type == "cuda" and isinstance(model, StackModel)
+            and args.grad_accum == 1 and not args.activation_offload)
+
+
 def train(args, model, parallel, ck, dataset, validation_dataset=None):
-    trainer = Trainer(args, model, parallel)
+    device = next(model.parameters()).device
+    graphed = use_graph_trainer(args, model, device)
+    if graphed:
+        from .flat import GraphTrainer
+        trainer = GraphTrainer(args, model, parallel)
+    else:
+        trainer = Trainer(args, model, parallel)
     opt, device = trainer.optimizer, trainer.device
     generator = torch.Generator().manual_seed(args.seed + 100 + parallel.dp_rank)
     start = 0
@@ -200,12 +212,17 @@ def train(args, model, parallel, ck, dataset, validation_dataset=None):
     stats = torch.zeros(3, device=device, dtype=torch.float64)
     window_start, window_steps = time.perf_counter(), 0
     for step in range(start, args.steps):
-        opt.zero_grad(set_to_none=True)
-        trainer.set_lr(step)
-        for micro in range(args.grad_accum):
+        if graphed:
             ids, target, mask, _ = make_batch(args, generator, dataset)
-            stats += trainer.micro_step(ids, target, mask, last=micro == args.grad_accum - 1).to(device)
-        norm = trainer.finish_step()
+            host, norm = trainer.step(ids, target, mask, args.lr * lr_factor(step, args.steps))
+            stats += host.to(device)
+        else:
+            opt.zero_grad(set_to_none=True)
+            trainer.set_lr(step)
+            for micro in range(args.grad_accum):
+                ids, target, mask, _ = make_batch(args, generator, dataset)
+                stats += trainer.micro_step(ids, target, mask, last=micro == args.grad_accum - 1).to(device)
+            norm = trainer.finish_step()
         window_steps += 1
         if (step + 1) % args.log_every == 0 or step == args.steps - 1:
             totals = sum_all(stats)
@@ -241,6 +258,8 @@ def train(args, model, parallel, ck, dataset, validation_dataset=None):
             emit({"event": "early_stop", "step": step + 1, "exact": round(record["exact"], 4)},
                  args, parallel.rank)
             break
+    if graphed:
+        trainer.close()
 
 
 @torch.no_grad()
@@ -389,9 +408,14 @@ def run(args):
         else:
             dataset = None
         model.to(device)
+        if device.type == "cuda" and isinstance(model, StackModel) and args.backend != "torch":
+            parallel.attach_fused(device)
         if args.command == "train":
             return train(args, model, parallel, ck, dataset, validation)
         return evaluate(args, model, parallel, dataset)
     finally:
+        parallel_ctx = locals().get("parallel")
+        if parallel_ctx is not None:
+            parallel_ctx.close()
         if dist.is_initialized():
             dist.destroy_process_group()

@@ -1,0 +1,378 @@
+"""Flat parameter storage, flat AdamW and the CUDA-graph training step.
+
+``FlatParameters`` moves every trainable parameter into one fp32 buffer
+(parameters become views), gradients into a second one and keeps a bf16
+shadow of the masters for the GEMMs. That makes three things one kernel or
+one collective each: the gradient reduction across ranks (one NCCL
+all-reduce, or reduce-scatter + all-gather under ZeRO-1), the gradient norm
+and the AdamW update (``csrc/fused/flat_optim.cu``), which also refreshes
+the bf16 shadow, so no per-step weight casts remain.
+
+``GraphTrainer`` captures one whole training micro-step (input copies from
+pinned memory, forward, backward, gradient reduction, clipping, AdamW and
+the statistics copy back to pinned memory) in a CUDA graph after two eager
+steps, then replays it. The step is host-sync free: the supervised width is
+the full shard (no data-dependent ``width``), the non-finite check and the
+clip coefficient are evaluated on the device (a non-finite step is skipped
+by the optimizer kernel and reported after the replay, as the eager path
+raises before applying it), and the learning rate and step count are read
+from device memory refreshed by an in-graph copy.
+
+The reference trains eagerly with DDP and torch AdamW
+(st/runtime/engine.py:85-119,160-190); it has no graph capture.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _native, fused
+
+ALIGN = 64            # elements: 256-byte aligned parameter views
+
+
+class FlatParameters:
+    """One fp32 buffer for the masters, one for gradients, a bf16 shadow."""
+
+    def __init__(self, model: torch.nn.Module, device: torch.device, shards: int = 1):
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        offsets, total = [], 0
+        for p in self.params:
+            offsets.append(total)
+            total += -(-p.numel() // ALIGN) * ALIGN
+        quantum = ALIGN * max(1, shards)
+        total = -(-total // quantum) * quantum
+        self.total, self.offsets = total, offsets
+        self.data = torch.zeros(total, device=device, dtype=torch.float32)
+        self.grad = torch.zeros(total, device=device, dtype=torch.float32)
+        self.shadow = torch.empty(total, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            for p, off in zip(self.params, offsets):
+                view = self.data[off:off + p.numel()].view_as(p)
+                view.copy_(p.detach())
+                p.data = view
+                p.grad = self.grad[off:off + p.numel()].view_as(p)
+            self.shadow.copy_(self.data)
+        for p, off in zip(self.params, offsets):
+            fused.register_shadow(p, self.shadow[off:off + p.numel()].view_as(p))
+
+    def zero_grad(self) -> None:
+        self.grad.zero_()
+
+    def release(self) -> None:
+        for p in self.params:
+            fused._shadows.pop(id(p), None)
+
+
+class GradBuckets:
+    """All-reduce of the flat gradient in contiguous buckets, overlapped with backward.
+
+    A post-accumulate hook on every parameter counts down its bucket; a
+    complete bucket is all-reduced asynchronously (NCCL stream) while the
+    backward pass continues. Buckets are launched strictly from the last one
+    down, so every rank issues the same collective sequence whatever order
+    its hooks fire in; ``finish()`` launches what is left (parameters without
+    a gradient this step) and makes the current stream wait for all of them.
+    Inside graph capture the hooks run once and the launches are recorded.
+    """
+
+    def __init__(self, flat: FlatParameters, group=None, bucket_bytes: int = 32 << 20):
+        self.flat, self.group = flat, group
+        limit = max(1, bucket_bytes // 4)
+        self.bounds, self.owner = [], {}
+        lo = 0
+        for i, (p, off) in enumerate(zip(flat.params, flat.offsets)):
+            end = off + -(-p.numel() // ALIGN) * ALIGN
+            if end - lo > limit and off > lo:
+                self.bounds.append((lo, off))
+                lo = off
+            self.owner[id(p)] = len(self.bounds)
+        self.bounds.append((lo, flat.total))
+        self.count = [0] * len(self.bounds)
+        for p in flat.params:
+            self.count[self.owner[id(p)]] += 1
+        self.handles = [p.register_post_accumulate_grad_hook(self._hook) for p in flat.params]
+        self.active = False
+
+    def start(self) -> None:
+        self.pending = list(self.count)
+        self.ready = [False] * len(self.bounds)
+        self.next = len(self.bounds) - 1
+        self.works = []
+        self.active = True
+
+    def _launch_ready(self) -> None:
+        while self.next >= 0 and self.ready[self.next]:
+            lo, hi = self.bounds[self.next]
+            self.works.append(dist.all_reduce(self.flat.grad[lo:hi], group=self.group, async_op=True))
+            self.next -= 1
+
+    def _hook(self, param) -> None:
+        if not self.active:
+            return
+        b = self.owner[id(param)]
+        self.pending[b] -= 1
+        if self.pending[b] == 0:
+            self.ready[b] = True
+            self._launch_ready()
+
+    def finish(self) -> None:
+        self.ready = [True] * len(self.bounds)
+        self._launch_ready()
+        for work in self.works:
+            work.wait()
+        self.works = []
+        self.active = False
+
+    def remove(self) -> None:
+        for h in self.handles:
+            h.remove()
+
+
+class FlatAdamW:
+    """AdamW over a flat buffer (optionally this rank's ZeRO-1 shard of it).
+
+    Hyper-parameters that change per step live in ``hyper`` on the device:
+    ``[lr, step, max_norm, grad_sq_norm]``.
+    """
+
+    def __init__(self, flat: FlatParameters, lr: float, betas=(0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.0, max_norm: float = 0.0, group=None, shard: bool = False):
+        self.flat = flat
+        cuda = flat.data.is_cuda
+        self.ext = _native.load(required=True) if cuda else _TorchFlat()
+        self.lr, self.betas, self.eps, self.weight_decay, self.max_norm = lr, betas, eps, weight_decay, max_norm
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.shard = shard and self.world > 1
+        n = flat.total // self.world if self.shard else flat.total
+        lo = self.rank * n if self.shard else 0
+        self.lo, self.n = lo, n
+        device = flat.data.device
+        self.exp_avg = torch.zeros(n, device=device)
+        self.exp_avg_sq = torch.zeros(n, device=device)
+        self.hyper = torch.zeros(4, device=device)
+        self.hyper_host = torch.zeros(4, pin_memory=cuda)
+        self.step_count = 0
+        self.grad_shard = torch.empty(n, device=device) if self.shard else None
+
+    def set_step(self, lr: float) -> None:
+        """Host side of a step: refreshes the pinned hyper-parameters (copied in-graph)."""
+        self.step_count += 1
+        self.hyper_host[0] = lr
+        self.hyper_host[1] = float(self.step_count)
+        self.hyper_host[2] = float(self.max_norm)
+
+    def load_hyper(self) -> None:
+        self.hyper.copy_(self.hyper_host, non_blocking=True)
+
+    def reduce_and_step(self, loss_check: torch.Tensor | None = None, reduced: bool = False) -> None:
+        """``reduced``: the gradient was already all-reduced (bucketed during backward)."""
+        flat = self.flat
+        if self.world > 1 and not reduced:
+            if self.shard:
+                dist.reduce_scatter_tensor(self.grad_shard, flat.grad, group=self.group)
+                grad = self.grad_shard
+            else:
+                dist.all_reduce(flat.grad, group=self.group)
+                grad = flat.grad
+        elif self.world > 1 and self.shard:
+            grad = flat.grad[self.lo:self.lo + self.n]
+        else:
+            grad = flat.grad
+        self.ext.flat_sq_norm(grad, self.hyper)
+        if self.shard:
+            dist.all_reduce(self.hyper[3:4], group=self.group)
+        data = flat.data[self.lo:self.lo + self.n]
+        shadow = flat.shadow[self.lo:self.lo + self.n]
+        self.ext.flat_adamw(data, grad, self.exp_avg, self.exp_avg_sq, shadow, self.hyper, loss_check,
+                            self.betas[0], self.betas[1], self.eps, self.weight_decay)
+        if self.shard:
+            dist.all_gather_into_tensor(flat.data, data, group=self.group)
+            dist.all_gather_into_tensor(flat.shadow, shadow, group=self.group)
+
+    def grad_norm(self) -> float:
+        return float(self.hyper[3].sqrt())
+
+    # -- checkpoints: torch.optim.AdamW layout (per-parameter state) ---------
+
+    def _full_moments(self):
+        if not self.shard:
+            return self.exp_avg, self.exp_avg_sq
+        full = []
+        for shard in (self.exp_avg, self.exp_avg_sq):
+            buf = torch.empty(self.flat.total, device=shard.device)
+            dist.all_gather_into_tensor(buf, shard, group=self.group)
+            full.append(buf)
+        return tuple(full)
+
+    def consolidate_state_dict(self, to: int = 0) -> None:
+        """Collective under sharding (every rank calls it, like ZeRO's)."""
+        self._consolidated = self._full_moments()
+
+    def state_dict(self) -> dict:
+        moments = getattr(self, "_consolidated", None) or self._full_moments()
+        self._consolidated = None
+        m, v = moments
+        state = {}
+        for i, (p, off) in enumerate(zip(self.flat.params, self.flat.offsets)):
+            state[i] = {"step": torch.tensor(float(self.step_count)),
+                        "exp_avg": m[off:off + p.numel()].view_as(p).detach().cpu().clone(),
+                        "exp_avg_sq": v[off:off + p.numel()].view_as(p).detach().cpu().clone()}
+        group = {"lr": self.lr, "betas": self.betas, "eps": self.eps, "weight_decay": self.weight_decay,
+                 "amsgrad": False, "maximize": False, "foreach": None, "capturable": False,
+                 "differentiable": False, "fused": None, "params": list(range(len(self.flat.params)))}
+        return {"state": state, "param_groups": [group]}
+
+    def load_state_dict(self, sd: dict) -> None:
+        device = self.exp_avg.device
+        m = torch.zeros(self.flat.total, device=device)
+        v = torch.zeros(self.flat.total, device=device)
+        steps = set()
+        for i, (p, off) in enumerate(zip(self.flat.params, self.flat.offsets)):
+            entry = sd["state"].get(i) or sd["state"].get(str(i))
+            if entry is None:
+                continue
+            m[off:off + p.numel()].copy_(entry["exp_avg"].reshape(-1))
+            v[off:off + p.numel()].copy_(entry["exp_avg_sq"].reshape(-1))
+            steps.add(int(float(entry["step"])))
+        self.exp_avg.copy_(m[self.lo:self.lo + self.n])
+        self.exp_avg_sq.copy_(v[self.lo:self.lo + self.n])
+        self.step_count = max(steps) if steps else 0
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        """Gradients are cleared inside the captured step."""
+
+
+class _TorchFlat:
+    """CPU arithmetic of the flat kernels (same formulas; used by the gloo tests)."""
+
+    @staticmethod
+    def flat_sq_norm(grad, hyper):
+        hyper[3] = grad.double().pow(2).sum().float()
+
+    @staticmethod
+    def flat_adamw(param, grad, exp_avg, exp_avg_sq, shadow, hyper, loss_check, beta1, beta2, eps, decay):
+        lr, step, max_norm, sq = (float(x) for x in hyper[:4])
+        check = float(loss_check) if loss_check is not None else 0.0
+        if not (torch.isfinite(torch.tensor(sq)) and torch.isfinite(torch.tensor(check))):
+            return
+        scale = min(max_norm / (sq ** 0.5 + 1e-6), 1.0) if max_norm > 0 else 1.0
+        g = grad * scale
+        bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
+        param.mul_(1 - lr * decay)
+        exp_avg.lerp_(g, 1 - beta1)
+        exp_avg_sq.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+        param.addcdiv_(exp_avg, exp_avg_sq.sqrt() / bc2 ** 0.5 + eps, value=-lr / bc1)
+        if shadow is not None:
+            shadow.copy_(param)
+
+
+class GraphTrainer:
+    """One micro-step per optimizer step, captured in a CUDA graph after two eager steps."""
+
+    EAGER_STEPS = 2
+
+    def __init__(self, args, model, parallel, use_graph: bool = True, overlap: bool = True):
+        if args.grad_accum != 1:
+            raise ValueError("the graph trainer runs one micro-step per optimizer step")
+        self.args, self.model, self.parallel = args, model, parallel
+        self.device = next(model.parameters()).device
+        group = None
+        shards = parallel.world_size if args.optimizer_shard else 1
+        self.flat = FlatParameters(model, self.device, shards)
+        self.optimizer = FlatAdamW(self.flat, args.lr, (0.9, 0.95), weight_decay=args.weight_decay,
+                                   max_norm=args.clip_grad, group=group, shard=args.optimizer_shard)
+        self.cuda = self.device.type == "cuda"
+        self.use_graph = use_graph and self.cuda
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        self.buckets = GradBuckets(self.flat) if world > 1 and overlap else None
+        self.graph = None
+        self.graph_launches = 0
+        self.calls = 0
+        self.static = None
+
+    def _buffers(self, ids, target, mask):
+        pinned = [t.pin_memory() if self.cuda else t.clone() for t in (ids, target, mask)]
+        device = [torch.empty_like(t, device=self.device) for t in pinned]
+        stats_host = torch.zeros(6, dtype=torch.float64, pin_memory=self.cuda)
+        return pinned, device, stats_host
+
+    def _body(self):
+        (ids_h, tgt_h, mask_h), (ids, tgt, mask), stats_host = self.static
+        opt, parallel = self.optimizer, self.parallel
+        opt.load_hyper()
+        ids.copy_(ids_h, non_blocking=True)
+        tgt.copy_(tgt_h, non_blocking=True)
+        mask.copy_(mask_h, non_blocking=True)
+        self.flat.zero_grad()
+        amp = torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.args.precision == "bf16",
+                             cache_enabled=False)
+        with amp:
+            result = self.model.forward_loss(ids, tgt, sup=mask, parallel=parallel, offset=self.offset,
+                                             static_width=True)
+        totals = torch.stack((result["loss_sum"].detach().float(), result["count"].float()))
+        if dist.is_initialized():
+            dist.all_reduce(totals)
+        loss = result["loss_sum"] / totals[1].clamp_min(1.0)
+        if self.buckets is not None:
+            self.buckets.start()
+        loss.backward()
+        if self.buckets is not None:
+            self.buckets.finish()
+        check = totals[0] / totals[1]               # non-finite (or 0/0 with no tokens) skips the update
+        opt.reduce_and_step(check, reduced=self.buckets is not None)
+        stats = torch.cat((torch.stack((result["loss_sum"].detach().double(), result["count"].double(),
+                                        result["correct"].double(), opt.hyper[3].double())),
+                           totals.double()))
+        stats_host.copy_(stats, non_blocking=True)
+
+    def step(self, ids, target, mask, lr: float):
+        """One optimizer step; returns host ``(loss_sum, count, correct)`` float64 and the grad norm."""
+        parallel = self.parallel
+        ids, self.offset = parallel.shard(ids, self.model.block_size)
+        target, _ = parallel.shard(target, self.model.block_size, -100)
+        mask, _ = parallel.shard(mask, self.model.block_size, False)
+        if self.static is None:
+            self.static = self._buffers(ids, target, mask)
+        (ids_h, tgt_h, mask_h), _, stats_host = self.static
+        ids_h.copy_(ids)
+        tgt_h.copy_(target)
+        mask_h.copy_(mask)
+        self.optimizer.set_step(lr)
+        if not self.use_graph:
+            self._body()
+        elif self.calls < self.EAGER_STEPS:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self._body()
+            torch.cuda.current_stream().wait_stream(side)
+        else:
+            if self.graph is None:
+                ext = _native.load(required=True)
+                before = ext.launch_count()
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph):
+                    self._body()
+                self.graph_launches = ext.launch_count() - before   # native kernels per replay
+            self.graph.replay()
+        self.calls += 1
+        if self.cuda:
+            torch.cuda.current_stream().synchronize()
+        stats = stats_host.clone()          # [loss_sum, count, correct, grad_sq_norm, global loss, global count]
+        if stats[5] == 0:
+            self.optimizer.step_count -= 1
+            raise ValueError("global batch has no supervised tokens")
+        if not bool(torch.isfinite(stats[4])) or not bool(torch.isfinite(stats[3])):
+            self.optimizer.step_count -= 1
+            raise FloatingPointError("non-finite loss across ranks; optimizer step was not applied")
+        return stats[:3], float(stats[3].sqrt())
+
+    def close(self) -> None:
+        """Release the graph before the process group goes away."""
+        self.graph = None
+        if self.buckets is not None:
+            self.buckets.remove()
+        self.flat.release()

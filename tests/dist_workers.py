@@ -98,3 +98,56 @@ def train_cp2(rank, world):
           "--backend", "torch", "--precision", "fp32", "--save", os.environ["TEST_SAVE"],
           "--context-parallel", os.environ["TEST_CP"], "--log-every", "1", "--grad-accum", "2"])
     return "finished"
+
+
+def _flat_vs_eager(parallel, shard):
+    """Three steps of the flat (graph-ready) trainer against the eager trainer."""
+    import copy
+    import torch
+    from exploration_b200 import ExecutionConfig, build_model
+    from exploration_b200.cli import parse_args
+    from exploration_b200.runtime.engine import Trainer, make_batch, lr_factor
+    from exploration_b200.runtime.flat import GraphTrainer
+    world = parallel.world_size
+    args = parse_args(["train", "--dim", "64", "--heads", "4", "--block-size", "8", "--arch", "Lx1,G",
+                       "--task", "random", "--length", str(64 * max(1, parallel.cp_size)),
+                       "--batch-size", "1", "--precision", "fp32", "--device", "cpu", "--backend", "torch",
+                       "--context-parallel", str(parallel.cp_size), "--steps", "3", "--save", "",
+                       "--clip-grad", "0.05", "--weight-decay", "0.1"] +
+                      (["--optimizer-shard"] if shard else ["--no-optimizer-shard"]))
+    torch.manual_seed(0)
+    options = {"model": "stack", "vocab_size": 256, "dim": 64, "heads": 4, "block_size": 8, "topk": 4,
+               "arch": "Lx1,G", "ffn_ratio": 2.0}
+    base = build_model(options, execution=ExecutionConfig(backend="torch"))
+    eager_model, flat_model = copy.deepcopy(base), copy.deepcopy(base)
+    eager = Trainer(args, eager_model, parallel)
+    flat = GraphTrainer(args, flat_model, parallel, use_graph=False)
+    gen_a = torch.Generator().manual_seed(5 + parallel.dp_rank)
+    gen_b = torch.Generator().manual_seed(5 + parallel.dp_rank)
+    for step in range(3):
+        lr = args.lr * lr_factor(step, args.steps)
+        eager.optimizer.zero_grad(set_to_none=True)
+        for group in eager.optimizer.param_groups:
+            group["lr"] = lr
+        ids, target, mask, _ = make_batch(args, gen_a)
+        a = eager.micro_step(ids, target, mask, last=True)
+        eager.finish_step()
+        ids, target, mask, _ = make_batch(args, gen_b)
+        b, _ = flat.step(ids, target, mask, lr)
+        assert torch.allclose(a, b, rtol=1e-5, atol=1e-5), (step, a, b)
+    for (name, p), q in zip(eager_model.named_parameters(), flat_model.parameters()):
+        assert torch.allclose(p, q, rtol=1e-4, atol=1e-6), name
+    flat.close()
+    return world
+
+
+def flat_trainer(rank, world):
+    import torch.distributed as dist
+    from exploration_b200.parallel.context import ParallelContext
+    cp = int(os.environ["TEST_CP"])
+    shard = os.environ.get("TEST_SHARD") == "1"
+    parallel = ParallelContext.initialize(cp, "cpu")
+    try:
+        return _flat_vs_eager(parallel, shard)
+    finally:
+        dist.destroy_process_group()

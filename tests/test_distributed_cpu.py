@@ -71,3 +71,11 @@ def test_injected_rank_failure_ends_every_rank():
     assert out.get(1, ("missing",))[0] == "error" and "injected fault" in out[1][1]
     # The healthy rank must not finish training: its next collective fails or times out.
     assert out.get(0, ("error", "no report"))[0] == "error"
+
+
+@pytest.mark.parametrize("cp,shard", [(2, "0"), (1, "1"), (2, "1")])
+def test_flat_trainer_matches_eager(cp, shard):
+    out = launch("flat_trainer", 2, {"TEST_CP": str(cp), "TEST_SHARD": shard})
+    assert len(out) == 2, out
+    for rank, (status, payload) in out.items():
+        assert status == "ok", payload
