@@ -121,7 +121,7 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   const uint32_t tmem = sm.tmem_base;
 
   // Tile-level bounds shared by every role.
-  int max_pos = -1, remote_end = 0, local_start = 1 << 30;
+  int max_pos = -1, remote_end = 0, local_start = 1 << 30, min_first_local = 1 << 30;
   for (int r = 0; r < kM; ++r) {
     const int pr_ = sm.pos[r];
     if (pr_ < 0) continue;
@@ -129,11 +129,15 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     const int first_local = (pr_ / B - 1) * B;   // may be negative: no remote keys
     remote_end = max(remote_end, first_local);
     local_start = min(local_start, max(first_local, 0));
+    min_first_local = min(min_first_local, first_local);
   }
   const int limit = min(p.keys, max_pos + 1);
   const int tiles = limit > 0 ? (limit + kN - 1) / kN : 0;
   auto remote_used = [&](int j) { return j * kN < remote_end; };
   auto local_used = [&](int j) { return max_pos >= 0 && j * kN + kN > local_start && j * kN <= max_pos; };
+  // Every key of tile j is an in-range remote key for every valid row of the
+  // CTA: no masks, no local state, finite scores.
+  auto pure_remote = [&](int j) { return (j + 1) * kN <= min_first_local && (j + 1) * kN <= p.keys; };
 
   if (warp == 0) {
     if (lane == 0 && tiles > 0) {
@@ -241,6 +245,81 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       }
       tc_wait_ld();
       const int k0 = j * kN;
+      if (pure_remote(j)) {
+        // Fast path (most tiles of a long sequence): block log-masses from
+        // raw scores with the scale folded into one FFMA per exponent.
+        const bool row_ok = pos >= 0;
+        float seg_max[kSeg], seg_lse[kSeg];
+        float tz = kNegInf, remote_max = kNegInf;
+#pragma unroll
+        for (int g = 0; g < kSeg; ++g) {
+          float m = e[g * B];
+#pragma unroll
+          for (int c = 1; c < B; ++c) m = fmaxf(m, e[g * B + c]);
+          const float ms = m * p.scale_log2;
+          float sum = 0.f;
+#pragma unroll
+          for (int c = 0; c < B; ++c) {
+            const float x = ex2(fmaf(e[g * B + c], p.scale_log2, -ms));
+            e[g * B + c] = x;
+            sum += x;
+          }
+          seg_max[g] = ms;
+          seg_lse[g] = ms + lg2(sum);
+          tz = log2_add(tz, seg_lse[g]);
+          remote_max = fmaxf(remote_max, ms + seg_lse[g]);
+        }
+        if (!row_ok) {
+          tz = kNegInf;
+          remote_max = kNegInf;
+        }
+        zr = log2_add(zr, tz);
+        float alpha_r = 1.f;
+        bool rescale = false;
+        if (remote_max > m_r + kRescaleThreshold || (m_r == kNegInf && remote_max != kNegInf)) {
+          alpha_r = (m_r == kNegInf) ? 0.f : ex2(m_r - remote_max);
+          rescale = d_r > 0.f;
+          m_r = remote_max;
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+          const bool waited = j == 0 || mbar_wait(&sm.o_done, (j - 1) & 1, abort, p.err, kSiteODone);
+          if (!__all_sync(0xffffffffu, waited)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(lane_addr + 256 + c, r);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_r);
+            tmem_st32(lane_addr + 256 + c, r);
+          }
+        }
+        d_r *= alpha_r;
+        float fr[kSeg];
+#pragma unroll
+        for (int g = 0; g < kSeg; ++g) {
+          fr[g] = row_ok ? ex2(seg_max[g] + seg_lse[g] - m_r) : 0.f;
+          if (row_ok) d_r += ex2(2.f * seg_lse[g] - m_r);
+        }
+#pragma unroll
+        for (int c0 = 0; c0 < kN; c0 += 32) {
+          uint32_t packed_r[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c = c0 + 2 * i;
+            packed_r[i] = pack_bf16(e[c] * fr[c / B], e[c + 1] * fr[(c + 1) / B]);
+          }
+          tmem_st16(lane_addr + buf * 128 + c0 / 2, packed_r);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[buf]);
+        continue;
+      }
       // Scaled base-2 logits; keys past N are -inf.
       float local_max = kNegInf;
 #pragma unroll

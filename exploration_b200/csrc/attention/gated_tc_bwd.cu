@@ -133,13 +133,54 @@ EB_DEVICE void load_row32(uint32_t addr, float (&x)[32]) {
   for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]);
 }
 
-// Calls sink(c0, p[32], da[32]) for c0 = 0, 32, 64, 96.
+// Calls sink(c0, p[32], da[32]) for c0 = 0, 32, 64, 96. `fast`: every key of
+// the tile is an in-range remote key for every live row of the CTA (no masks,
+// finite scores), so the block log-masses come from raw scores with the scale
+// folded into one FFMA per exponent and no local terms exist.
 template <int B, typename Sink>
 EB_DEVICE void grad_row(uint32_t s_addr, uint32_t dp_addr, int k0, int keys, const RowStats& st,
-                        float scale_log2, float scale, Sink&& sink) {
+                        float scale_log2, float scale, bool fast, Sink&& sink) {
   const bool live = st.pos >= 0;
   if constexpr (B <= 32) {
     constexpr int kSeg = 32 / B;
+    if (fast) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < kT; c0 += 32) {
+        float a[32], dp[32], p[32], da[32];
+        load_row32(s_addr + c0, a);
+        load_row32(dp_addr + c0, dp);
+#pragma unroll
+        for (int g = 0; g < kSeg; ++g) {
+          float m = a[g * B];
+#pragma unroll
+          for (int i = 1; i < B; ++i) m = fmaxf(m, a[g * B + i]);
+          const float ms = m * scale_log2;
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < B; ++i) {
+            const float e = ex2(fmaf(a[g * B + i], scale_log2, -ms));
+            a[g * B + i] = e;
+            sum += e;
+          }
+          const float sb = ms + lg2(sum);
+          const float f = live ? ex2(ms + sb - st.zr2 - st.lse2) : 0.f;
+          float rb = 0.f;
+#pragma unroll
+          for (int i = 0; i < B; ++i) {
+            const float pv = a[g * B + i] * f;
+            const float direct = pv * (dp[g * B + i] - st.delta);
+            p[g * B + i] = pv;
+            da[g * B + i] = direct;
+            rb += direct;
+          }
+          const float gate = live ? ex2(ms - sb) * rb - ex2(ms - st.zr2) * st.rho : 0.f;
+#pragma unroll
+          for (int i = 0; i < B; ++i) da[g * B + i] = (da[g * B + i] + a[g * B + i] * gate) * scale;
+        }
+        sink(c0, p, da);
+      }
+      return;
+    }
 #pragma unroll 1
     for (int c0 = 0; c0 < kT; c0 += 32) {
       float a[32], dp[32], p[32], da[32];
@@ -403,7 +444,8 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         break;
       }
       tc_fence_after();
-      grad_row<B>(lane_addr, lane_addr + 128, j * kT, p.keys, st, p.scale_log2, p.scale,
+      const bool fast = (j + 1) * kT <= bnd[2] && (j + 1) * kT <= p.keys;
+      grad_row<B>(lane_addr, lane_addr + 128, j * kT, p.keys, st, p.scale_log2, p.scale, fast,
                   [&](int c0, const float (&pv)[32], const float (&da)[32]) {
                     uint32_t packed[16];
 #pragma unroll
@@ -574,7 +616,9 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         break;
       }
       tc_fence_after();
-      grad_row<B>(lane_addr, lane_addr + 128, k0, p.keys, st, p.scale_log2, p.scale,
+      const int local_start_i = p.bounds[(static_cast<int64_t>(batch) * p.q_tiles + i) * 3 + 2];
+      const bool fast = k0 + kT <= local_start_i && k0 + kT <= p.keys;
+      grad_row<B>(lane_addr, lane_addr + 128, k0, p.keys, st, p.scale_log2, p.scale, fast,
                   [&](int c0, const float (&pv)[32], const float (&da)[32]) {
                     const int box = c0 / 64, chunk0 = (c0 % 64) / 8;
 #pragma unroll

@@ -18,6 +18,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "../common/util.cuh"
 
 namespace eb {
@@ -308,12 +312,22 @@ size_t bwd_smem(int b, int D) {
 }
 
 std::pair<at::Tensor, at::Tensor> rope_tables(int block, int dim, const at::Device& device) {
-  // Offsets -b .. 2b-1; float32 angles as in the torch reference.
+  // Offsets -b .. 2b-1; float32 angles as in the torch reference. Built once
+  // per (device, block, dim) and kept, so no host->device copy happens inside
+  // a captured CUDA graph.
+  static std::mutex lock;
+  static std::map<std::tuple<int, int, int>, std::pair<at::Tensor, at::Tensor>> cache;
+  const std::lock_guard<std::mutex> guard(lock);
+  const auto key = std::make_tuple(static_cast<int>(device.index()), block, dim);
+  auto hit = cache.find(key);
+  if (hit != cache.end()) return hit->second;
   auto offsets = at::arange(-block, 2 * block, at::TensorOptions().dtype(at::kFloat));
   auto index = at::arange(0, dim, 2, at::TensorOptions().dtype(at::kFloat));
   auto inv = at::pow(10000.0, -index / static_cast<double>(dim));
   auto angles = offsets.unsqueeze(1) * inv.unsqueeze(0);
-  return {angles.cos().to(device).contiguous(), angles.sin().to(device).contiguous()};
+  auto value = std::make_pair(angles.cos().to(device).contiguous(), angles.sin().to(device).contiguous());
+  cache.emplace(key, value);
+  return value;
 }
 
 }  // namespace

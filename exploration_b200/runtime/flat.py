@@ -32,20 +32,38 @@ ALIGN = 64            # elements: 256-byte aligned parameter views
 
 
 class FlatParameters:
-    """One fp32 buffer for the masters, one for gradients, a bf16 shadow."""
+    """One fp32 buffer for the masters, one for gradients, a bf16 shadow.
+
+    Layout: ``[replicated | sharded]``. Parameters the model reads in fp32
+    (norms, biases, embeddings: anything that is not only a GEMM operand) come
+    first and are updated on every rank; the GEMM weights follow and, under
+    ZeRO-1, each rank updates only its equal slice of them, after which the
+    bf16 shadows (all the forward pass reads of those weights) are
+    all-gathered. Their fp32 masters are gathered only when a checkpoint
+    needs them (``gather_masters``).
+    """
 
     def __init__(self, model: torch.nn.Module, device: torch.device, shards: int = 1):
-        self.params = [p for p in model.parameters() if p.requires_grad]
+        params = [p for p in model.parameters() if p.requires_grad]
+        fp32_read = {id(m.weight) for m in model.modules() if isinstance(m, torch.nn.Embedding)}
+        small = [p for p in params if p.dim() < 2 or id(p) in fp32_read]
+        big = [p for p in params if not (p.dim() < 2 or id(p) in fp32_read)]
+        self.params = small + big
+        quantum = ALIGN * max(1, shards)
         offsets, total = [], 0
-        for p in self.params:
+        for i, p in enumerate(self.params):
+            if i == len(small):
+                total = -(-total // quantum) * quantum
             offsets.append(total)
             total += -(-p.numel() // ALIGN) * ALIGN
-        quantum = ALIGN * max(1, shards)
-        total = -(-total // quantum) * quantum
+        if not big:
+            total = -(-total // quantum) * quantum
+        self.split = offsets[len(small)] if big else total
+        total = self.split + -(-(total - self.split) // quantum) * quantum
         self.total, self.offsets = total, offsets
         self.data = torch.zeros(total, device=device, dtype=torch.float32)
         self.grad = torch.zeros(total, device=device, dtype=torch.float32)
-        self.shadow = torch.empty(total, device=device, dtype=torch.bfloat16)
+        self.shadow = torch.zeros(total, device=device, dtype=torch.bfloat16)
         with torch.no_grad():
             for p, off in zip(self.params, offsets):
                 view = self.data[off:off + p.numel()].view_as(p)
@@ -130,32 +148,37 @@ class GradBuckets:
 
 
 class FlatAdamW:
-    """AdamW over a flat buffer (optionally this rank's ZeRO-1 shard of it).
+    """AdamW over a flat buffer; under ZeRO-1 over this rank's slice of the sharded region.
 
     Hyper-parameters that change per step live in ``hyper`` on the device:
     ``[lr, step, max_norm, grad_sq_norm]``.
     """
 
     def __init__(self, flat: FlatParameters, lr: float, betas=(0.9, 0.95), eps: float = 1e-8,
-                 weight_decay: float = 0.0, max_norm: float = 0.0, group=None, shard: bool = False):
+                 weight_decay: float = 0.0, max_norm: float = 0.0, group=None, shard: bool = False,
+                 shadow_only: bool = False):
+        """``shadow_only``: the model reads the sharded weights only through their bf16
+        shadows (native bf16 path), so only the shadows are all-gathered each step."""
         self.flat = flat
+        self.shadow_only = shadow_only
         cuda = flat.data.is_cuda
         self.ext = _native.load(required=True) if cuda else _TorchFlat()
         self.lr, self.betas, self.eps, self.weight_decay, self.max_norm = lr, betas, eps, weight_decay, max_norm
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        self.shard = shard and self.world > 1
-        n = flat.total // self.world if self.shard else flat.total
-        lo = self.rank * n if self.shard else 0
-        self.lo, self.n = lo, n
+        self.shard = shard and self.world > 1 and flat.split < flat.total
+        split = flat.split if self.shard else flat.total
+        n = (flat.total - split) // self.world if self.shard else 0
+        self.split, self.lo, self.n = split, split + self.rank * n, n
         device = flat.data.device
-        self.exp_avg = torch.zeros(n, device=device)
-        self.exp_avg_sq = torch.zeros(n, device=device)
+        # Moments: the replicated region in full, then this rank's slice of the sharded one.
+        self.exp_avg = torch.zeros(split + n, device=device)
+        self.exp_avg_sq = torch.zeros(split + n, device=device)
         self.hyper = torch.zeros(4, device=device)
+        self.hyper_small = torch.zeros(4, device=device)
         self.hyper_host = torch.zeros(4, pin_memory=cuda)
         self.step_count = 0
-        self.grad_shard = torch.empty(n, device=device) if self.shard else None
 
     def set_step(self, lr: float) -> None:
         """Host side of a step: refreshes the pinned hyper-parameters (copied in-graph)."""
@@ -167,30 +190,48 @@ class FlatAdamW:
     def load_hyper(self) -> None:
         self.hyper.copy_(self.hyper_host, non_blocking=True)
 
+    def _regions(self):
+        """(data, grad, exp_avg, exp_avg_sq, shadow) views per updated region."""
+        f, a, b = self.flat, self.exp_avg, self.exp_avg_sq
+        out = [(f.data[:self.split], f.grad[:self.split], a[:self.split], b[:self.split],
+                f.shadow[:self.split])] if self.split else []
+        if self.shard:
+            lo, hi = self.lo, self.lo + self.n
+            out.append((f.data[lo:hi], f.grad[lo:hi], a[self.split:], b[self.split:], f.shadow[lo:hi]))
+        return out
+
     def reduce_and_step(self, loss_check: torch.Tensor | None = None, reduced: bool = False) -> None:
         """``reduced``: the gradient was already all-reduced (bucketed during backward)."""
         flat = self.flat
         if self.world > 1 and not reduced:
-            if self.shard:
-                dist.reduce_scatter_tensor(self.grad_shard, flat.grad, group=self.group)
-                grad = self.grad_shard
-            else:
-                dist.all_reduce(flat.grad, group=self.group)
-                grad = flat.grad
-        elif self.world > 1 and self.shard:
-            grad = flat.grad[self.lo:self.lo + self.n]
-        else:
-            grad = flat.grad
-        self.ext.flat_sq_norm(grad, self.hyper)
+            dist.all_reduce(flat.grad, group=self.group)
+        regions = self._regions()
         if self.shard:
+            # |g|^2 = replicated part (same on every rank) + sum over ranks of their slices.
+            self.ext.flat_sq_norm(regions[-1][1], self.hyper)
             dist.all_reduce(self.hyper[3:4], group=self.group)
-        data = flat.data[self.lo:self.lo + self.n]
-        shadow = flat.shadow[self.lo:self.lo + self.n]
-        self.ext.flat_adamw(data, grad, self.exp_avg, self.exp_avg_sq, shadow, self.hyper, loss_check,
-                            self.betas[0], self.betas[1], self.eps, self.weight_decay)
+            if self.split:
+                self.ext.flat_sq_norm(regions[0][1], self.hyper_small)
+                self.hyper[3:4].add_(self.hyper_small[3:4])
+        else:
+            self.ext.flat_sq_norm(flat.grad, self.hyper)
+        for data, grad, m, v, shadow in regions:
+            self.ext.flat_adamw(data, grad, m, v, shadow, self.hyper, loss_check,
+                                self.betas[0], self.betas[1], self.eps, self.weight_decay)
         if self.shard:
-            dist.all_gather_into_tensor(flat.data, data, group=self.group)
-            dist.all_gather_into_tensor(flat.shadow, shadow, group=self.group)
+            mine = flat.shadow[self.lo:self.lo + self.n]      # in place: NCCL accepts send == recv slot
+            dist.all_gather_into_tensor(flat.shadow[self.split:], mine if mine.is_cuda else mine.clone(),
+                                        group=self.group)
+            if not self.shadow_only:
+                self.gather_masters()
+
+    def gather_masters(self) -> None:
+        """Collective: make every rank's fp32 masters of the sharded region current."""
+        if self.shard:
+            flat = self.flat
+            mine = flat.data[self.lo:self.lo + self.n]
+            dist.all_gather_into_tensor(flat.data[self.split:], mine if mine.is_cuda else mine.clone(),
+                                        group=self.group)
 
     def grad_norm(self) -> float:
         return float(self.hyper[3].sqrt())
@@ -201,14 +242,16 @@ class FlatAdamW:
         if not self.shard:
             return self.exp_avg, self.exp_avg_sq
         full = []
-        for shard in (self.exp_avg, self.exp_avg_sq):
-            buf = torch.empty(self.flat.total, device=shard.device)
-            dist.all_gather_into_tensor(buf, shard, group=self.group)
+        for moment in (self.exp_avg, self.exp_avg_sq):
+            buf = torch.zeros(self.flat.total, device=moment.device)
+            buf[:self.split].copy_(moment[:self.split])
+            dist.all_gather_into_tensor(buf[self.split:], moment[self.split:].clone(), group=self.group)
             full.append(buf)
         return tuple(full)
 
     def consolidate_state_dict(self, to: int = 0) -> None:
-        """Collective under sharding (every rank calls it, like ZeRO's)."""
+        """Collective under sharding (every rank calls it, like ZeRO's): moments and masters."""
+        self.gather_masters()
         self._consolidated = self._full_moments()
 
     def state_dict(self) -> dict:
@@ -237,8 +280,10 @@ class FlatAdamW:
             m[off:off + p.numel()].copy_(entry["exp_avg"].reshape(-1))
             v[off:off + p.numel()].copy_(entry["exp_avg_sq"].reshape(-1))
             steps.add(int(float(entry["step"])))
-        self.exp_avg.copy_(m[self.lo:self.lo + self.n])
-        self.exp_avg_sq.copy_(v[self.lo:self.lo + self.n])
+        for full, mine in ((m, self.exp_avg), (v, self.exp_avg_sq)):
+            mine[:self.split].copy_(full[:self.split])
+            if self.shard:
+                mine[self.split:].copy_(full[self.lo:self.lo + self.n])
         self.step_count = max(steps) if steps else 0
 
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -282,8 +327,11 @@ class GraphTrainer:
         group = None
         shards = parallel.world_size if args.optimizer_shard else 1
         self.flat = FlatParameters(model, self.device, shards)
+        native_bf16 = (self.device.type == "cuda" and args.precision == "bf16"
+                       and getattr(model, "backend", "auto") != "torch")
         self.optimizer = FlatAdamW(self.flat, args.lr, (0.9, 0.95), weight_decay=args.weight_decay,
-                                   max_norm=args.clip_grad, group=group, shard=args.optimizer_shard)
+                                   max_norm=args.clip_grad, group=group, shard=args.optimizer_shard,
+                                   shadow_only=native_bf16)
         self.cuda = self.device.type == "cuda"
         self.use_graph = use_graph and self.cuda
         world = dist.get_world_size() if dist.is_initialized() else 1

@@ -3,7 +3,7 @@
 ``FusedAdamW`` keeps PyTorch's AdamW state layout (``step``, ``exp_avg``,
 ``exp_avg_sq`` per parameter and the standard ``param_groups``), so its state
 dict is interchangeable with ``torch.optim.AdamW`` in checkpoints. On CUDA
-one kernel of the extension (``csrc/fused/adamw.cu``) updates every fp32
+one kernel of the extension (``csrc/fused/loss_optim.cu``) updates every fp32
 master parameter of a group: decoupled weight decay, both moment updates,
 bias correction and the optional gradient-clipping scale are one pass over
 memory. CPU parameters use the same arithmetic in torch.
@@ -16,6 +16,7 @@ from __future__ import annotations
 import math
 
 import torch
+from torch.autograd.graph import increment_version
 from torch.optim import Optimizer
 
 from ..ops import _native
@@ -87,6 +88,10 @@ class FusedAdamW(Optimizer):
                        [self.state[p]["exp_avg_sq"] for p in params],
                        float(group["lr"]), float(beta1), float(beta2), float(group["eps"]),
                        float(group["weight_decay"]), float(bc1), float(bc2), float(self.grad_scale))
+        # The kernel writes through raw pointers; bump the version counters so
+        # caches keyed on them (the bf16 weight copies) see the update.
+        for p in params:
+            increment_version(p)
         record("adamw_step", tensors=len(params))
 
 

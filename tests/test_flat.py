@@ -11,12 +11,16 @@ def test_flat_parameters_are_views():
                          "topk": 4, "arch": "Lx1,G", "ffn_ratio": 2.0}, execution=ExecutionConfig(backend="torch"))
     before = {n: p.detach().clone() for n, p in model.named_parameters()}
     flat = FlatParameters(model, torch.device("cpu"), shards=4)
-    assert flat.total % (64 * 4) == 0
-    for (name, p), off in zip(model.named_parameters(), flat.offsets):
-        assert torch.equal(p, before[name])
+    assert flat.split % (64 * 4) == 0 and (flat.total - flat.split) % (64 * 4) == 0
+    names = {id(p): n for n, p in model.named_parameters()}
+    assert len(flat.params) == len(names)
+    for p, off in zip(flat.params, flat.offsets):
+        assert torch.equal(p, before[names[id(p)]])
         assert p.data_ptr() == flat.data[off:].data_ptr()
         assert p.grad.data_ptr() == flat.grad[off:].data_ptr()
         assert off % 64 == 0
+        # fp32-read parameters (norms, biases, embeddings) sit before the split
+        assert (off < flat.split) == (p.dim() < 2 or p is model.embedding.weight)
     flat.data.add_(1.0)
     assert all(torch.equal(p, before[n] + 1) for n, p in model.named_parameters())
     flat.release()
