@@ -28,6 +28,7 @@ SOURCES = [
     "fused/flat_optim.cu",
     "attention/local_halo.cu",
     "attention/local_halo_b16.cu",
+    "attention/local_tc.cu",
     "attention/gated_entry.cu",
     "attention/gated_simt.cu",
     "attention/gated_tc.cu",

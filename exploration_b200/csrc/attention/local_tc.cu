@@ -1,0 +1,336 @@
+// Local halo window attention on the 5th-generation tensor cores: block 16,
+// head dim 64, bf16 (the shape of every Stack preset), sm_100a.
+//
+// Same semantics as local_halo.cu: query row t of block g attends causally
+// to keys of blocks g-1 and g (the previous block comes from `prev` at a
+// chunk start, or is masked), keys limited to [valid_start, start + n), RoPE
+// applied on load relative to the window (only query/key distances enter
+// the scores, so the CTA origin is used: 16 rows before its first query).
+//
+// Forward, one CTA = 128 query rows of one (batch, head):
+//   warp 0      TMA: Q [128 x 64], K and V [144 x 64] (halo block + 128
+//               rows; a chunk start reads the halo from `prev`, or zero fill)
+//   warps 4-7   rotate Q and K in shared memory (128-byte swizzled rows)
+//   warp 1      S = Q K^T for all 128 x 144 (query, key) pairs into TMEM
+//               (the band is 32 keys wide; the extra columns cost nothing
+//               that matters at this size), then O = P V with P read from
+//               TMEM (A-from-TMEM MMA form)
+//   warps 4-7   thread = query row: softmax over its 32-key window, P (bf16,
+//               normalised, zeros outside the window) written back to TMEM,
+//               then the epilogue stores O and the row's log-sum-exp.
+// TMEM: S / P columns [0, 144), O [160, 224); 256 columns per CTA, two CTAs
+// per SM.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <map>
+#include <mutex>
+
+#include "../common/sm100.cuh"
+#include "../common/tma.cuh"
+
+namespace eb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kB = 16;
+constexpr int kD = 64;
+constexpr int kM = 128;                 // query rows per CTA
+constexpr int kKeys = kM + kB;          // 144 key rows per CTA
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kOCol = 160;
+constexpr int kTable = kM + 2 * kB;     // rotation offsets 0 .. 159
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct LtArgs {
+  int n, heads;
+  int64_t start, valid_start;
+  int has_prev;
+  const float* cos;    // [kTable, 32]
+  const float* sin;
+  __nv_bfloat16* out;  // [B, n, H * 64]
+  float* lse;          // [B, n, H]
+  ErrorSlot* err;
+};
+
+struct alignas(1024) LtSmem {
+  __nv_bfloat16 q[kM * kD];
+  __nv_bfloat16 k[kKeys * kD];
+  __nv_bfloat16 v[kKeys * kD];
+  uint64_t q_full, k_full, v_full, rot_done, s_full, p_full, o_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+EB_DEVICE bool key_ok(const LtArgs& a, int t) {
+  if (t < 0 && !a.has_prev) return false;
+  return t < a.n && a.start + t >= a.valid_start;
+}
+
+// Rotate rows [0, rows) of a 64-wide bf16 tile stored with the 128-byte
+// swizzle (row r at r * 128 bytes, 16-byte chunk c at chunk c ^ (r & 7)) by
+// the RoPE angle of offset (r + off0): dims d and d + 32 form a pair.
+EB_DEVICE void rotate_tile(__nv_bfloat16* tile, int rows, int off0, const float* cos_t, const float* sin_t,
+                           int tid, int nthreads) {
+  uint8_t* base = reinterpret_cast<uint8_t*>(tile);
+  for (int item = tid; item < rows * 4; item += nthreads) {
+    const int r = item >> 2, c = item & 3;
+    uint4* lo = reinterpret_cast<uint4*>(base + r * 128 + ((c ^ (r & 7)) << 4));
+    uint4* hi = reinterpret_cast<uint4*>(base + r * 128 + (((c + 4) ^ (r & 7)) << 4));
+    uint4 a = *lo, b = *hi;
+    __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+    __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&b);
+    const float* cs = cos_t + (r + off0) * 32 + 8 * c;
+    const float* sn = sin_t + (r + off0) * 32 + 8 * c;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x1 = __bfloat1622float2(pa[i]), x2 = __bfloat1622float2(pb[i]);
+      const float c0 = cs[2 * i], c1 = cs[2 * i + 1], s0 = sn[2 * i], s1 = sn[2 * i + 1];
+      pa[i] = __floats2bfloat162_rn(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+      pb[i] = __floats2bfloat162_rn(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+    }
+    *lo = a;
+    *hi = b;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+local_tc_fwd_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
+                    const __grid_constant__ CUtensorMap t_prev, LtArgs a) {
+  extern __shared__ __align__(1024) uint8_t raw_smem[];
+  LtSmem& sm = *reinterpret_cast<LtSmem*>((reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int t0 = blockIdx.x * kM;
+  volatile int* abort = &sm.abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.k_full, 1);
+    mbar_init(&sm.v_full, 1);
+    mbar_init(&sm.rot_done, 128);
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.o_full, 1);
+    sm.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) tmem_alloc(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const int H = a.heads;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&t_main);
+      prefetch_tensormap(&t_halo);
+      const bool from_prev = t0 == 0 && a.has_prev;
+      if (from_prev) prefetch_tensormap(&t_prev);
+      mbar_expect_tx(&sm.q_full, kM * kD * 2);
+      tma_load_4d(sm.q, &t_main, &sm.q_full, 0, head, t0, batch);
+      for (int part = 1; part <= 2; ++part) {
+        uint64_t* bar = part == 1 ? &sm.k_full : &sm.v_full;
+        __nv_bfloat16* dst = part == 1 ? sm.k : sm.v;
+        mbar_expect_tx(bar, kKeys * kD * 2);
+        if (from_prev) tma_load_4d(dst, &t_prev, bar, 0, part * H + head, 0, batch);
+        else tma_load_4d(dst, &t_halo, bar, 0, part * H + head, t0 - kB, batch);   // zero fill before row 0
+        tma_load_4d(dst + kB * kD, &t_main, bar, 0, part * H + head, t0, batch);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&sm.rot_done, 0, abort, a.err, kSiteQFull);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t id_s = idesc_bf16(kM, kKeys, false, false);
+        const uint32_t q_addr = smem_u32(sm.q), k_addr = smem_u32(sm.k);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem, smem_desc_sw128(q_addr + kk * 32, 16, 1024), smem_desc_sw128(k_addr + kk * 32, 16, 1024), id_s,
+                 kk > 0);
+        tc_commit(&sm.s_full);
+        ok = mbar_wait(&sm.v_full, 0, abort, a.err, kSiteKvFull) && mbar_wait(&sm.p_full, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t id_pv = idesc_bf16(kM, kD, false, true);
+        const uint32_t v_addr = smem_u32(sm.v);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)
+          mma_ts(tmem + kOCol, tmem + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kKeys * 128, 1024), id_pv, kk > 0);
+        tc_commit(&sm.o_full);
+      }
+    }
+  } else if (warp >= 4) {
+    const int tid = threadIdx.x - 128;
+    const int w = warp - 4;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
+    // 1. Rotate Q (offsets 16..143) and K (0..143) in place.
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull) &&
+                                          mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+    if (ok) {
+      rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
+      rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive(&sm.rot_done);
+    // 2. Softmax of row r over its window: keys 16 * (r / 16) .. + 31 (CTA key index).
+    const int r = tid;
+    const int t = t0 + r;
+    const int off = lane >= 16 ? kB : 0;     // window start relative to the warp's first column 32 w
+    float lse_row = kNegInf;
+    float p[48];
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.s_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      uint32_t s0[32], s1[16];
+      tmem_ld32(lane_addr + 32 * w, s0);
+      tmem_ld16(lane_addr + 32 * w + 32, s1);
+      tc_wait_ld();
+      const float scale = 0.125f * kLog2e;
+      float m = kNegInf;
+#pragma unroll
+      for (int j = 0; j < 48; ++j) {
+        const int kk = 32 * w + j;                   // CTA key index; token t0 - 16 + kk
+        const bool in = j >= off && j < off + 2 * kB && kk <= r + kB && key_ok(a, t0 - kB + kk) && t < a.n;
+        const float x = __uint_as_float(j < 32 ? s0[j] : s1[j - 32]) * scale;
+        p[j] = in ? x : kNegInf;
+        m = fmaxf(m, p[j]);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 48; ++j) {
+        p[j] = m == kNegInf ? 0.f : ex2(p[j] - m);
+        sum += p[j];
+      }
+      const float inv = sum > 0.f ? 1.f / sum : 0.f;
+#pragma unroll
+      for (int j = 0; j < 48; ++j) p[j] *= inv;
+      lse_row = sum > 0.f ? (m + lg2(sum)) * kLn2 : kNegInf;
+      // P as bf16 pairs over all 144 key columns (72 TMEM columns): the band
+      // of this warp is pair columns [16 w, 16 w + 24), the rest is zero.
+      {
+        uint32_t zero[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) zero[i] = 0u;
+#pragma unroll
+        for (int chunk = 0; chunk < kKeys / 16; ++chunk)
+          if (chunk < 2 * w || chunk > 2 * w + 2) tmem_st8(lane_addr + chunk * 8, zero);
+      }
+#pragma unroll
+      for (int rel = 0; rel < 3; ++rel) {            // band chunks 2w .. 2w+2 (16 keys each)
+        uint32_t packed[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) packed[i] = pack_bf16(p[rel * 16 + 2 * i], p[rel * 16 + 2 * i + 1]);
+        tmem_st8(lane_addr + (2 * w + rel) * 8, packed);
+      }
+      tc_wait_st();
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.p_full);
+    // 3. Epilogue: O rows (already normalised) and the row's log-sum-exp.
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.o_full, 0, abort, a.err, kSiteODone));
+    if (ok) {
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      tmem_ld32(lane_addr + kOCol, o0);
+      tmem_ld32(lane_addr + kOCol + 32, o1);
+      tc_wait_ld();
+      if (t < a.n) {
+        uint4* dst = reinterpret_cast<uint4*>(a.out + ((static_cast<int64_t>(batch) * a.n + t) * H + head) * kD);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t* src = c < 4 ? o0 + 8 * c : o1 + 8 * (c - 4);
+          dst[c] = make_uint4(pack_bf16(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                              pack_bf16(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                              pack_bf16(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                              pack_bf16(__uint_as_float(src[6]), __uint_as_float(src[7])));
+        }
+        a.lse[(static_cast<int64_t>(batch) * a.n + t) * H + head] = lse_row;
+      }
+    }
+  }
+  // A CTA that gave up waits for its own copies before leaving.
+  if (warp == 0 && lane == 0 && *abort) {
+    mbar_wait(&sm.q_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.k_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.v_full, 0, abort, nullptr, kSiteDrain);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+std::pair<at::Tensor, at::Tensor> tc_tables(const at::Device& device) {
+  static std::mutex lock;
+  static std::map<int, std::pair<at::Tensor, at::Tensor>> cache;
+  const std::lock_guard<std::mutex> guard(lock);
+  auto hit = cache.find(device.index());
+  if (hit != cache.end()) return hit->second;
+  auto offsets = at::arange(0, kTable, at::TensorOptions().dtype(at::kFloat));
+  auto index = at::arange(0, kD, 2, at::TensorOptions().dtype(at::kFloat));
+  auto inv = at::pow(10000.0, -index / static_cast<double>(kD));
+  auto angles = offsets.unsqueeze(1) * inv.unsqueeze(0);
+  auto value = std::make_pair(angles.cos().to(device).contiguous(), angles.sin().to(device).contiguous());
+  cache.emplace(device.index(), value);
+  return value;
+}
+
+// qkv [B, n, 3, H, 64] viewed as (64, 3H, n, B); boxes of 64 x 1 x rows x 1.
+CUtensorMap qkv_map(const void* base, int batch, int n, int heads, int rows) {
+  return make_bhld_map(const_cast<void*>(base), batch, n, 3 * heads, kD, rows);
+}
+
+}  // namespace
+
+bool local_tc_supported(const at::Tensor& qkv, int64_t block) {
+  return qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && block == kB && qkv.size(-1) == kD &&
+         qkv.is_contiguous();
+}
+
+std::vector<at::Tensor> local_tc_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& prev, int64_t start,
+                                     int64_t valid_start, int64_t n) {
+  TORCH_CHECK(local_tc_supported(qkv, kB), "local_tc_fwd: contiguous bf16 [B, n, 3, H, 64] with block 16");
+  const int batch = qkv.size(0), heads = qkv.size(3);
+  TORCH_CHECK(qkv.size(1) == n && qkv.size(2) == 3, "local_tc_fwd: qkv must be [B, n, 3, H, 64]");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  auto out = at::empty({batch, n, heads * kD}, qkv.options());
+  auto lse = at::empty({batch, n, heads}, qkv.options().dtype(at::kFloat));
+  if (n == 0) return {out, lse};
+  auto tables = tc_tables(qkv.device());
+  const bool has_prev = prev.has_value() && prev->defined();
+  at::Tensor prev_c;
+  if (has_prev) {
+    prev_c = prev->contiguous();
+    TORCH_CHECK(prev_c.scalar_type() == at::kBFloat16 && prev_c.size(0) == batch && prev_c.size(1) == kB &&
+                    prev_c.size(2) == 3 && prev_c.size(3) == heads && prev_c.size(4) == kD,
+                "local_tc_fwd: prev must be [B, 16, 3, H, 64] bf16");
+  }
+  CUtensorMap t_main = qkv_map(qkv.data_ptr(), batch, n, heads, kM);
+  CUtensorMap t_halo = qkv_map(qkv.data_ptr(), batch, n, heads, kB);
+  CUtensorMap t_prev = has_prev ? qkv_map(prev_c.data_ptr(), batch, kB, heads, kB) : t_halo;
+  LtArgs args{static_cast<int>(n), heads, start, valid_start, has_prev ? 1 : 0,
+              tables.first.data_ptr<float>(), tables.second.data_ptr<float>(),
+              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(),
+              device_error_slot(qkv.device().index())};
+  // At least ~80 KB of shared memory per CTA keeps two CTAs per SM (TMEM: 2 x 256 columns).
+  const size_t smem = std::max<size_t>(sizeof(LtSmem) + 1024, 80 * 1024);
+  auto kernel = local_tc_fwd_kernel;
+  EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid((n + kM - 1) / kM, heads, batch);
+  kernel<<<grid, kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(t_main, t_halo, t_prev, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(1);
+  return {out, lse};
+}
+
+}  // namespace eb

@@ -69,6 +69,9 @@ void flat_adamw(at::Tensor& param, const at::Tensor& grad, at::Tensor& exp_avg, 
                 const c10::optional<at::Tensor>& loss_check, double beta1, double beta2, double eps,
                 double decay);
 void flat_cast_bf16(const at::Tensor& x, at::Tensor& out);
+bool local_tc_supported(const at::Tensor& qkv, int64_t block);
+std::vector<at::Tensor> local_tc_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& prev, int64_t start,
+                                     int64_t valid_start, int64_t n);
 std::vector<at::Tensor> sparse_pop(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                    const at::Tensor& pos, const at::Tensor& ids, const at::Tensor& scores,
                                    const at::Tensor& log_zr, int64_t block, int64_t offset);
@@ -120,6 +123,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flat_sq_norm", &eb::flat_sq_norm, "hyper[3] = sum of squares of a flat fp32 buffer");
   m.def("flat_adamw", &eb::flat_adamw, "AdamW over a flat buffer with device-side lr/step/clip");
   m.def("flat_cast_bf16", &eb::flat_cast_bf16);
+  m.def("local_tc_supported", &eb::local_tc_supported);
+  m.def("local_tc_fwd", &eb::local_tc_fwd, "tcgen05 local halo attention forward (block 16, head dim 64, bf16)");
   m.def("launch_count", &eb::launch_count, "kernels launched by this extension so far");
   m.def("device_errors", &device_errors, "read and clear (site, cta) of the last bounded-wait timeout");
 }

@@ -273,8 +273,12 @@ class _LocalAttentionNative(torch.autograd.Function):
         ext = _native.native(qkv)
         qkv = qkv.contiguous()
         prev = None if qkv_prev is None else qkv_prev.contiguous()
-        out, lse = ext.local_attention_fwd(qkv, prev, start, valid_start, n, block)
-        record("local_attention_fwd", block=block, head_dim=qkv.shape[-1], dtype=str(qkv.dtype))
+        if ext.local_tc_supported(qkv, block):
+            out, lse = ext.local_tc_fwd(qkv, prev, start, valid_start, n)
+            record("local_attention_fwd", block=block, head_dim=qkv.shape[-1], dtype=str(qkv.dtype), path="tcgen05")
+        else:
+            out, lse = ext.local_attention_fwd(qkv, prev, start, valid_start, n, block)
+            record("local_attention_fwd", block=block, head_dim=qkv.shape[-1], dtype=str(qkv.dtype))
         ctx.save_for_backward(qkv, prev if prev is not None else qkv.new_empty(0), out, lse)
         ctx.has_prev = prev is not None
         ctx.meta = (start, valid_start, n, block)

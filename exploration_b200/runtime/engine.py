@@ -31,6 +31,7 @@ from .. import data
 from ..api import build_model
 from ..config import ExecutionConfig, ModelConfig
 from ..data.tokens import TokenDataset, enwik8_dataset
+from ..ops import fused
 from ..models.baseline import BaselineModel
 from ..models.stack import StackModel
 from ..parallel.context import ParallelContext, init_distributed, sum_all
@@ -162,6 +163,9 @@ class Trainer:
         norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.args.clip_grad,
                                               error_if_nonfinite=True)
         self.optimizer.step()
+        # Parameters changed (locally, or by a ZeRO broadcast that bypasses the
+        # version counters): drop the per-step low-precision weight copies.
+        fused.clear_cast_cache()
         return norm
 
 
