@@ -34,6 +34,7 @@ SOURCES = [
     "attention/gated_tc.cu",
     "attention/gated_tc_bwd.cu",
     "sparse/sparse_read.cu",
+    "sparse/block_scores_tc.cu",
     "gemm/gemm_tc.cu",
     "comm/symm_heap.cu",
 ]

@@ -19,7 +19,7 @@
 //               normalised, zeros outside the window) written back to TMEM,
 //               then the epilogue stores O and the row's log-sum-exp.
 // TMEM: S / P columns [0, 144), O [160, 224); 256 columns per CTA, two CTAs
-// per SM.
+// per SM. The backward kernels are described below.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -270,6 +270,501 @@ local_tc_fwd_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
   }
 }
 
+// ---------------------------------------------------------------------------
+// backward
+//
+// dQ kernel (query owner), one CTA = 128 query rows of one (batch, head):
+//   S = Q K^T and dP = dO V^T (128 x 144 each, sequentially in the same TMEM
+//   columns), P = exp(S - lse) from the forward's log-sum-exp, dS = P (dP -
+//   delta) on the 32-key window (bf16 into TMEM), dQ = dS K (A-from-TMEM),
+//   then RoPE is undone on dQ. delta = rowsum(dO o O) is formed here and
+//   stored for the key kernel.
+// dK/dV kernel (key owner), one CTA = 128 key rows [s0, s0+128); its
+//   queries are [s0, s0+144) (the next block also sees the last key block):
+//   S^T = K Q^T and dP^T = V dO^T (128 x 144), P^T and dS^T on the window,
+//   dV = P^T dO and dK = dS^T Q (both A-from-TMEM), RoPE undone on dK. An
+//   extra CTA owns the halo block (`prev`), whose gradient goes to dprev.
+// Every element is written by exactly one CTA: no atomics, deterministic.
+// ---------------------------------------------------------------------------
+
+struct LtBwdArgs {
+  int n, heads;
+  int64_t start, valid_start;
+  int has_prev;
+  const float* cos;
+  const float* sin;
+  const __nv_bfloat16* out;     // [B, n, H * 64]
+  const __nv_bfloat16* dout;
+  const float* lse;             // [B, n, H]
+  float* delta;                 // [B, n, H] (written by the dQ kernel)
+  __nv_bfloat16* dqkv;          // [B, n, 3, H, 64]
+  __nv_bfloat16* dprev;         // [B, 16, 3, H, 64] or nullptr
+  ErrorSlot* err;
+};
+
+struct alignas(1024) LtDqSmem {
+  __nv_bfloat16 q[kM * kD];
+  __nv_bfloat16 g[kM * kD];     // dO
+  __nv_bfloat16 k[kKeys * kD];
+  __nv_bfloat16 v[kKeys * kD];
+  uint64_t q_full, g_full, k_full, v_full, rot_done, s_full, s_read, dp_full, ds_full, dq_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+EB_DEVICE bool bwd_key_ok(const LtBwdArgs& a, int t) {
+  if (t < 0 && !a.has_prev) return false;
+  return t < a.n && a.start + t >= a.valid_start;
+}
+
+// RoPE backward on a 64-wide fp32 row held as 64 values: x = R(-theta) y.
+EB_DEVICE void unrotate_row(float (&y)[64], int offset, const float* cos_t, const float* sin_t) {
+  const float* cs = cos_t + offset * 32;
+  const float* sn = sin_t + offset * 32;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float a = y[i], b = y[i + 32], c = cs[i], s = sn[i];
+    y[i] = a * c + b * s;
+    y[i + 32] = b * c - a * s;
+  }
+}
+
+EB_DEVICE void store_row64(__nv_bfloat16* dst, const float (&y)[64]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    d[c] = make_uint4(pack_bf16(y[8 * c], y[8 * c + 1]), pack_bf16(y[8 * c + 2], y[8 * c + 3]),
+                      pack_bf16(y[8 * c + 4], y[8 * c + 5]), pack_bf16(y[8 * c + 6], y[8 * c + 7]));
+}
+
+EB_DEVICE void load_tmem64(uint32_t addr, float (&y)[64]) {
+  uint32_t r0[32], r1[32];
+  tmem_ld32(addr, r0);
+  tmem_ld32(addr + 32, r1);
+  tc_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    y[i] = __uint_as_float(r0[i]);
+    y[i + 32] = __uint_as_float(r1[i]);
+  }
+}
+
+// 48 fp32 TMEM columns starting at `addr` (the warp's band).
+EB_DEVICE void load_band48(uint32_t addr, float (&x)[48]) {
+  uint32_t r0[32], r1[16];
+  tmem_ld32(addr, r0);
+  tmem_ld16(addr + 32, r1);
+  tc_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r0[j]);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) x[32 + j] = __uint_as_float(r1[j]);
+}
+
+// 48 band values as bf16 pairs into the 72 pair columns at `addr` (zeros
+// outside this warp's band: pair columns [16 w, 16 w + 24)).
+EB_DEVICE void store_band_bf16(uint32_t addr, int w, const float (&x)[48]) {
+  uint32_t zero[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) zero[i] = 0u;
+#pragma unroll
+  for (int chunk = 0; chunk < kKeys / 16; ++chunk)
+    if (chunk < 2 * w || chunk > 2 * w + 2) tmem_st8(addr + chunk * 8, zero);
+#pragma unroll
+  for (int rel = 0; rel < 3; ++rel) {
+    uint32_t packed[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) packed[i] = pack_bf16(x[rel * 16 + 2 * i], x[rel * 16 + 2 * i + 1]);
+    tmem_st8(addr + (2 * w + rel) * 8, packed);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+local_tc_dq_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
+                   const __grid_constant__ CUtensorMap t_prev, const __grid_constant__ CUtensorMap t_dout,
+                   LtBwdArgs a) {
+  extern __shared__ __align__(1024) uint8_t raw_smem[];
+  LtDqSmem& sm = *reinterpret_cast<LtDqSmem*>((reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int t0 = blockIdx.x * kM;
+  const int H = a.heads;
+  volatile int* abort = &sm.abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.g_full, 1);
+    mbar_init(&sm.k_full, 1);
+    mbar_init(&sm.v_full, 1);
+    mbar_init(&sm.rot_done, 128);
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_read, 128);
+    mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.dq_full, 1);
+    sm.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) tmem_alloc(&sm.tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&t_main);
+      prefetch_tensormap(&t_halo);
+      prefetch_tensormap(&t_dout);
+      const bool from_prev = t0 == 0 && a.has_prev;
+      mbar_expect_tx(&sm.q_full, kM * kD * 2);
+      tma_load_4d(sm.q, &t_main, &sm.q_full, 0, head, t0, batch);
+      mbar_expect_tx(&sm.g_full, kM * kD * 2);
+      tma_load_4d(sm.g, &t_dout, &sm.g_full, 0, head, t0, batch);
+      for (int part = 1; part <= 2; ++part) {
+        uint64_t* bar = part == 1 ? &sm.k_full : &sm.v_full;
+        __nv_bfloat16* dst = part == 1 ? sm.k : sm.v;
+        mbar_expect_tx(bar, kKeys * kD * 2);
+        if (from_prev) tma_load_4d(dst, &t_prev, bar, 0, part * H + head, 0, batch);
+        else tma_load_4d(dst, &t_halo, bar, 0, part * H + head, t0 - kB, batch);
+        tma_load_4d(dst + kB * kD, &t_main, bar, 0, part * H + head, t0, batch);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16(kM, kKeys, false, false);
+      const uint32_t id_dq = idesc_bf16(kM, kD, false, true);
+      bool ok = mbar_wait(&sm.rot_done, 0, abort, a.err, kSiteQFull);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sm.q), k_addr = smem_u32(sm.k);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem, smem_desc_sw128(q_addr + kk * 32, 16, 1024), smem_desc_sw128(k_addr + kk * 32, 16, 1024), id_s,
+                 kk > 0);
+        tc_commit(&sm.s_full);
+        ok = mbar_wait(&sm.g_full, 0, abort, a.err, kSiteKvFull) && mbar_wait(&sm.v_full, 0, abort, a.err, kSiteKvFull) &&
+             mbar_wait(&sm.s_read, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t g_addr = smem_u32(sm.g), v_addr = smem_u32(sm.v);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem, smem_desc_sw128(g_addr + kk * 32, 16, 1024), smem_desc_sw128(v_addr + kk * 32, 16, 1024), id_s,
+                 kk > 0);
+        tc_commit(&sm.dp_full);
+        ok = mbar_wait(&sm.ds_full, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)
+          mma_ts(tmem + kOCol, tmem + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kKeys * 128, 1024), id_dq, kk > 0);
+        tc_commit(&sm.dq_full);
+      }
+    }
+  } else if (warp >= 4) {
+    const int tid = threadIdx.x - 128;
+    const int w = warp - 4;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull) &&
+                                          mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+    if (ok) {
+      rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
+      rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive(&sm.rot_done);
+    // Row statistics: lse (base 2) and delta = dO . O (stored for the key kernel).
+    const int r = tid, t = t0 + r;
+    const bool row_ok = t < a.n;
+    float lse2 = 0.f, delta = 0.f;
+    if (row_ok) {
+      const int64_t s = (static_cast<int64_t>(batch) * a.n + t) * H + head;
+      const float l = a.lse[s];
+      lse2 = l == kNegInf ? 0.f : l * kLog2e;
+      const uint4* go = reinterpret_cast<const uint4*>(a.dout + s * kD);
+      const uint4* oo = reinterpret_cast<const uint4*>(a.out + s * kD);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 gu = go[c], ou = oo[c];
+        const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gu);
+        const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&ou);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 gf = __bfloat1622float2(gp[i]), of = __bfloat1622float2(op[i]);
+          delta += gf.x * of.x + gf.y * of.y;
+        }
+      }
+      a.delta[s] = delta;
+    }
+    const int off = lane >= 16 ? kB : 0;
+    float p[48];
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.s_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      float x[48];
+      load_band48(lane_addr + 32 * w, x);
+      const float scale = 0.125f * kLog2e;
+#pragma unroll
+      for (int j = 0; j < 48; ++j) {
+        const int kk = 32 * w + j;
+        const bool in = row_ok && j >= off && j < off + 2 * kB && kk <= r + kB && bwd_key_ok(a, t0 - kB + kk);
+        p[j] = in ? ex2(fmaf(x[j], scale, -lse2)) : 0.f;
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.s_read);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      float dp[48];
+      load_band48(lane_addr + 32 * w, dp);
+#pragma unroll
+      for (int j = 0; j < 48; ++j) dp[j] = p[j] * (dp[j] - delta);
+      store_band_bf16(lane_addr, w, dp);
+      tc_wait_st();
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.ds_full);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dq_full, 0, abort, a.err, kSiteODone));
+    if (ok) {
+      tc_fence_after();
+      float y[64];
+      load_tmem64(lane_addr + kOCol, y);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) y[i] *= 0.125f;
+      unrotate_row(y, r + kB, a.cos, a.sin);
+      if (row_ok) store_row64(a.dqkv + ((static_cast<int64_t>(batch) * a.n + t) * 3 * H + head) * kD, y);
+    }
+  }
+  if (warp == 0 && lane == 0 && *abort) {
+    mbar_wait(&sm.q_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.g_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.k_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.v_full, 0, abort, nullptr, kSiteDrain);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+struct alignas(1024) LtDkvSmem {
+  __nv_bfloat16 k[kM * kD];
+  __nv_bfloat16 v[kM * kD];
+  __nv_bfloat16 q[kKeys * kD];     // query rows s0 .. s0 + 143
+  __nv_bfloat16 g[kKeys * kD];     // dO rows s0 .. s0 + 143
+  float lse2[kKeys], delta[kKeys];
+  uint64_t k_full, v_full, q_full, g_full, rot_done, s_full, dp_full, p_full, ds_full, dv_full, dk_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr uint32_t kDkvTmemCols = 512;
+constexpr uint32_t kColDp = 160, kColDs = 160, kColDv = 320, kColDk = 384;
+
+__global__ void __launch_bounds__(kThreads, 1)
+local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
+                    const __grid_constant__ CUtensorMap t_prev, const __grid_constant__ CUtensorMap t_dout,
+                    const __grid_constant__ CUtensorMap t_dout16, LtBwdArgs a, int owner_ctas) {
+  extern __shared__ __align__(1024) uint8_t raw_smem[];
+  LtDkvSmem& sm = *reinterpret_cast<LtDkvSmem*>((reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const bool halo_cta = static_cast<int>(blockIdx.x) >= owner_ctas;   // keys of `prev`: rows s0 + 112 .. s0 + 127
+  const int s0 = halo_cta ? -kM : static_cast<int>(blockIdx.x) * kM;
+  const int H = a.heads;
+  volatile int* abort = &sm.abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.k_full, 1);
+    mbar_init(&sm.v_full, 1);
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.g_full, 1);
+    mbar_init(&sm.rot_done, 128);
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.dv_full, 1);
+    mbar_init(&sm.dk_full, 1);
+    sm.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) tmem_alloc(&sm.tmem_base, kDkvTmemCols);
+  // Per-query statistics of rows s0 .. s0 + 143 (base-2 lse, delta).
+  for (int i = threadIdx.x; i < kKeys; i += kThreads) {
+    const int t = s0 + i;
+    float l2 = 0.f, d = 0.f;
+    if (t >= 0 && t < a.n) {
+      const int64_t s = (static_cast<int64_t>(batch) * a.n + t) * H + head;
+      const float l = a.lse[s];
+      l2 = l == kNegInf ? 0.f : l * kLog2e;
+      d = a.delta[s];
+    }
+    sm.lse2[i] = l2;
+    sm.delta[i] = d;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&t_main);
+      prefetch_tensormap(&t_halo);
+      prefetch_tensormap(&t_dout);
+      prefetch_tensormap(&t_dout16);
+      for (int part = 1; part <= 2; ++part) {
+        uint64_t* bar = part == 1 ? &sm.k_full : &sm.v_full;
+        __nv_bfloat16* dst = part == 1 ? sm.k : sm.v;
+        mbar_expect_tx(bar, kM * kD * 2);
+        if (halo_cta) {
+          // Rows -128 .. -17 do not exist (zero fill, one 16-row box each);
+          // rows -16 .. -1 are the halo block `prev`.
+          for (int j = 0; j < kM / kB - 1; ++j)
+            tma_load_4d(dst + j * kB * kD, &t_halo, bar, 0, part * H + head, s0 + j * kB, batch);
+          tma_load_4d(dst + (kM - kB) * kD, &t_prev, bar, 0, part * H + head, 0, batch);
+        } else {
+          tma_load_4d(dst, &t_main, bar, 0, part * H + head, s0, batch);
+        }
+      }
+      mbar_expect_tx(&sm.q_full, kKeys * kD * 2);
+      tma_load_4d(sm.q, &t_main, &sm.q_full, 0, head, s0, batch);
+      tma_load_4d(sm.q + kM * kD, &t_halo, &sm.q_full, 0, head, s0 + kM, batch);
+      mbar_expect_tx(&sm.g_full, kKeys * kD * 2);
+      tma_load_4d(sm.g, &t_dout, &sm.g_full, 0, head, s0, batch);
+      tma_load_4d(sm.g + kM * kD, &t_dout16, &sm.g_full, 0, head, s0 + kM, batch);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16(kM, kKeys, false, false);
+      const uint32_t id_acc = idesc_bf16(kM, kD, false, true);
+      // dP^T = V dO^T needs no rotation: issue it first.
+      bool ok = mbar_wait(&sm.v_full, 0, abort, a.err, kSiteKvFull) && mbar_wait(&sm.g_full, 0, abort, a.err, kSiteKvFull);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sm.v), g_addr = smem_u32(sm.g);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem + kColDp, smem_desc_sw128(v_addr + kk * 32, 16, 1024), smem_desc_sw128(g_addr + kk * 32, 16, 1024),
+                 id_s, kk > 0);
+        tc_commit(&sm.dp_full);
+        ok = mbar_wait(&sm.rot_done, 0, abort, a.err, kSiteQFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k), q_addr = smem_u32(sm.q);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem, smem_desc_sw128(k_addr + kk * 32, 16, 1024), smem_desc_sw128(q_addr + kk * 32, 16, 1024), id_s,
+                 kk > 0);
+        tc_commit(&sm.s_full);
+        ok = mbar_wait(&sm.p_full, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t g_addr = smem_u32(sm.g);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)   // dV = P^T dO
+          mma_ts(tmem + kColDv, tmem + kk * 8, smem_desc_sw128(g_addr + kk * 2048, kKeys * 128, 1024), id_acc, kk > 0);
+        tc_commit(&sm.dv_full);
+        ok = mbar_wait(&sm.ds_full, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sm.q);
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk)   // dK = dS^T Q
+          mma_ts(tmem + kColDk, tmem + kColDs + kk * 8, smem_desc_sw128(q_addr + kk * 2048, kKeys * 128, 1024), id_acc,
+                 kk > 0);
+        tc_commit(&sm.dk_full);
+      }
+    }
+  } else if (warp >= 4) {
+    const int tid = threadIdx.x - 128;
+    const int w = warp - 4;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull) &&
+                                          mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
+    if (ok) {
+      // Origin 16 rows before s0: key row k at offset k + 16, query row i at i + 16.
+      rotate_tile(sm.k, kM, kB, a.cos, a.sin, tid, 128);
+      rotate_tile(sm.q, kKeys, kB, a.cos, a.sin, tid, 128);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive(&sm.rot_done);
+    const int kr = tid, tk = s0 + kr;              // key row and token
+    const bool key_live = bwd_key_ok(a, tk) && (!halo_cta || kr >= kM - kB);
+    const int off = lane >= 16 ? kB : 0;           // query window start relative to column 32 w
+    float p[48];
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.s_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      float x[48];
+      load_band48(lane_addr + 32 * w, x);
+      const float scale = 0.125f * kLog2e;
+#pragma unroll
+      for (int j = 0; j < 48; ++j) {
+        const int qi = 32 * w + j, tq = s0 + qi;   // query index in [0, 144) and token
+        const bool in = key_live && j >= off && j < off + 2 * kB && qi >= kr && tq >= 0 && tq < a.n;
+        p[j] = in ? ex2(fmaf(x[j], scale, -sm.lse2[qi])) : 0.f;
+      }
+      store_band_bf16(lane_addr, w, p);            // P^T over S^T's columns
+      tc_wait_st();
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.p_full);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      float dp[48];
+      load_band48(lane_addr + kColDp + 32 * w, dp);
+#pragma unroll
+      for (int j = 0; j < 48; ++j) dp[j] = p[j] * (dp[j] - sm.delta[32 * w + j]);
+      store_band_bf16(lane_addr + kColDs, w, dp);  // dS^T over dP^T's columns
+      tc_wait_st();
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.ds_full);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dv_full, 0, abort, a.err, kSiteODone) &&
+                                           mbar_wait(&sm.dk_full, 0, abort, a.err, kSiteODone));
+    if (ok) {
+      tc_fence_after();
+      float y[64];
+      __nv_bfloat16* base = nullptr;
+      if (halo_cta) {
+        if (kr >= kM - kB) base = a.dprev + ((static_cast<int64_t>(batch) * kB + (kr - (kM - kB))) * 3 * H + head) * kD;
+      } else if (tk < a.n) {
+        base = a.dqkv + ((static_cast<int64_t>(batch) * a.n + tk) * 3 * H + head) * kD;
+      }
+      load_tmem64(lane_addr + kColDv, y);
+      if (base) store_row64(base + 2 * H * kD, y);
+      load_tmem64(lane_addr + kColDk, y);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) y[i] *= 0.125f;
+      unrotate_row(y, kr + kB, a.cos, a.sin);
+      if (base) store_row64(base + H * kD, y);
+    }
+  }
+  if (warp == 0 && lane == 0 && *abort) {
+    mbar_wait(&sm.k_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.v_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.q_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.g_full, 0, abort, nullptr, kSiteDrain);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kDkvTmemCols);
+  }
+}
+
 std::pair<at::Tensor, at::Tensor> tc_tables(const at::Device& device) {
   static std::mutex lock;
   static std::map<int, std::pair<at::Tensor, at::Tensor>> cache;
@@ -331,6 +826,61 @@ std::vector<at::Tensor> local_tc_fwd(const at::Tensor& qkv, const c10::optional<
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(1);
   return {out, lse};
+}
+
+
+std::vector<at::Tensor> local_tc_bwd(const at::Tensor& dout, const at::Tensor& qkv, const c10::optional<at::Tensor>& prev,
+                                     const at::Tensor& out, const at::Tensor& lse, int64_t start, int64_t valid_start,
+                                     int64_t n) {
+  TORCH_CHECK(local_tc_supported(qkv, kB), "local_tc_bwd: contiguous bf16 [B, n, 3, H, 64] with block 16");
+  const int batch = qkv.size(0), heads = qkv.size(3);
+  TORCH_CHECK(dout.is_contiguous() && dout.scalar_type() == at::kBFloat16 && dout.sizes() == out.sizes() &&
+                  out.is_contiguous() && lse.is_contiguous(), "local_tc_bwd: dout/out [B, n, H*64] bf16");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  auto dqkv = at::empty_like(qkv);
+  const bool has_prev = prev.has_value() && prev->defined();
+  at::Tensor prev_c, dprev;
+  if (has_prev) {
+    prev_c = prev->contiguous();
+    dprev = at::zeros_like(prev_c);
+  }
+  if (n == 0) return {dqkv, dprev};
+  // The q part of dqkv is fully written by the dQ kernel and the k/v parts by
+  // the key kernel; dprev's q part stays zero.
+  auto delta = at::empty({batch, n, heads}, qkv.options().dtype(at::kFloat));
+  auto tables = tc_tables(qkv.device());
+  CUtensorMap t_main = qkv_map(qkv.data_ptr(), batch, n, heads, kM);
+  CUtensorMap t_halo = qkv_map(qkv.data_ptr(), batch, n, heads, kB);
+  CUtensorMap t_prev = has_prev ? qkv_map(prev_c.data_ptr(), batch, kB, heads, kB) : t_halo;
+  CUtensorMap t_dout = make_bhld_map(dout.data_ptr(), batch, n, heads, kD, kM);
+  CUtensorMap t_dout16 = make_bhld_map(dout.data_ptr(), batch, n, heads, kD, kB);
+  LtBwdArgs args{static_cast<int>(n), heads, start, valid_start, has_prev ? 1 : 0,
+                 tables.first.data_ptr<float>(), tables.second.data_ptr<float>(),
+                 reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+                 reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), lse.data_ptr<float>(),
+                 delta.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
+                 has_prev ? reinterpret_cast<__nv_bfloat16*>(dprev.data_ptr()) : nullptr,
+                 device_error_slot(qkv.device().index())};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int ctas = (n + kM - 1) / kM;
+  {
+    const size_t smem = std::max<size_t>(sizeof(LtDqSmem) + 1024, 80 * 1024);
+    auto kernel = local_tc_dq_kernel;
+    EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<dim3(ctas, heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout, args);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  {
+    // One CTA per SM: the kernel holds all 512 TMEM columns.
+    const size_t smem = std::max<size_t>(sizeof(LtDkvSmem) + 1024, 120 * 1024);
+    auto kernel = local_tc_dkv_kernel;
+    EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<dim3(ctas + (has_prev ? 1 : 0), heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout,
+                                                                                       t_dout16, args, ctas);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  count_launch(2);
+  return {dqkv, dprev};
 }
 
 }  // namespace eb

@@ -72,6 +72,12 @@ void flat_cast_bf16(const at::Tensor& x, at::Tensor& out);
 bool local_tc_supported(const at::Tensor& qkv, int64_t block);
 std::vector<at::Tensor> local_tc_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& prev, int64_t start,
                                      int64_t valid_start, int64_t n);
+std::vector<at::Tensor> local_tc_bwd(const at::Tensor& dout, const at::Tensor& qkv, const c10::optional<at::Tensor>& prev,
+                                     const at::Tensor& out, const at::Tensor& lse, int64_t start, int64_t valid_start,
+                                     int64_t n);
+bool block_scores_tc_supported(const at::Tensor& q, const at::Tensor& k, int64_t block, int64_t topk);
+std::vector<at::Tensor> block_scores_topk_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& pos,
+                                             int64_t block, int64_t first, int64_t topk);
 std::vector<at::Tensor> sparse_pop(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                    const at::Tensor& pos, const at::Tensor& ids, const at::Tensor& scores,
                                    const at::Tensor& log_zr, int64_t block, int64_t offset);
@@ -125,6 +131,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flat_cast_bf16", &eb::flat_cast_bf16);
   m.def("local_tc_supported", &eb::local_tc_supported);
   m.def("local_tc_fwd", &eb::local_tc_fwd, "tcgen05 local halo attention forward (block 16, head dim 64, bf16)");
+  m.def("local_tc_bwd", &eb::local_tc_bwd, "tcgen05 local halo attention backward (dQ kernel + dK/dV kernel)");
+  m.def("block_scores_tc_supported", &eb::block_scores_tc_supported);
+  m.def("block_scores_topk_tc", &eb::block_scores_topk_tc,
+        "tcgen05 exact block scores with log Z_R and a radix-select top-k per row");
   m.def("launch_count", &eb::launch_count, "kernels launched by this extension so far");
   m.def("device_errors", &device_errors, "read and clear (site, cta) of the last bounded-wait timeout");
 }

@@ -290,8 +290,12 @@ class _LocalAttentionNative(torch.autograd.Function):
         qkv, prev, out, lse = ctx.saved_tensors
         ext = _native.native(qkv)
         start, valid_start, n, block = ctx.meta
-        dqkv, dprev = ext.local_attention_bwd(grad.contiguous(), qkv, prev if ctx.has_prev else None,
-                                              out, lse, start, valid_start, n, block)
+        if ext.local_tc_supported(qkv, block) and grad.dtype == torch.bfloat16:
+            dqkv, dprev = ext.local_tc_bwd(grad.contiguous(), qkv, prev if ctx.has_prev else None,
+                                           out, lse, start, valid_start, n)
+        else:
+            dqkv, dprev = ext.local_attention_bwd(grad.contiguous(), qkv, prev if ctx.has_prev else None,
+                                                  out, lse, start, valid_start, n, block)
         return dqkv, (dprev if ctx.has_prev else None), None, None, None, None
 
 

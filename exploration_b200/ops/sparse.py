@@ -164,6 +164,18 @@ def _global_logsumexp(x, group):
 # ----------------------------------------------------------------------------
 
 @torch.inference_mode()
+def _score_chunks(cache, device, tile, native):
+    """``(first token, keys)`` pieces to score: a cache resident on the device in
+    one pass (the native scorer streams any length), otherwise page by page in
+    tiles of ``tile`` tokens."""
+    if native and isinstance(cache, TensorPages) and cache.k.device == device and cache.k.is_contiguous():
+        yield cache.offset, cache.k
+        return
+    for start, keys, _ in cache.pages(device, keys_only=True):
+        for lo in range(0, keys.shape[1], tile):
+            yield start + lo, keys[:, lo:lo + tile]
+
+
 def sparse_attention(q, cache, positions, block_size, topk, backend="auto", group=None,
                      score_page_tokens=65536, return_selection=False):
     """Exact scoring, global top-k, gate and sparse pop over a paged KV cache.
@@ -187,23 +199,25 @@ def sparse_attention(q, cache, positions, block_size, topk, backend="auto", grou
     tile = max(b, score_page_tokens // b * b)
     pos32 = positions.to(torch.int32).contiguous() if native else None
     qc = q.contiguous()
-    for start, keys, _ in cache.pages(q.device, keys_only=True):
-        for lo in range(0, keys.shape[1], tile):
-            chunk = keys[:, lo:lo + tile]
-            first = start + lo
-            if native:
-                part_scores, part_ids, part_zr = ext.block_scores_topk(
-                    qc, chunk.contiguous(), pos32, b, first, topk)
-                record("block_scores_topk", dtype=str(q.dtype), head_dim=q.shape[-1], block=b)
-                part_scores = part_scores.to(dtype)
-            else:
-                s = block_scores_reference(q, chunk, positions, b, first)
-                part_zr = s.logsumexp(-1)
-                count = min(topk, s.shape[-1])
-                part_scores, part_ids = s.topk(count, -1)
-                part_ids = part_ids + first // b
-            log_zr = torch.logaddexp(log_zr, part_zr.to(dtype))
-            scores, ids = _topk_merge(scores, ids, part_scores, part_ids.to(torch.int64), topk)
+    for first, chunk in _score_chunks(cache, q.device, tile, native):
+        if native and ext.block_scores_tc_supported(qc, chunk, b, topk):
+            part_scores, part_ids, part_zr = ext.block_scores_topk_tc(
+                qc, chunk.contiguous(), pos32, b, first, topk)
+            record("block_scores_topk", dtype=str(q.dtype), head_dim=q.shape[-1], block=b, path="tcgen05")
+            part_scores = part_scores.to(dtype)
+        elif native:
+            part_scores, part_ids, part_zr = ext.block_scores_topk(
+                qc, chunk.contiguous(), pos32, b, first, topk)
+            record("block_scores_topk", dtype=str(q.dtype), head_dim=q.shape[-1], block=b)
+            part_scores = part_scores.to(dtype)
+        else:
+            s = block_scores_reference(q, chunk, positions, b, first)
+            part_zr = s.logsumexp(-1)
+            count = min(topk, s.shape[-1])
+            part_scores, part_ids = s.topk(count, -1)
+            part_ids = part_ids + first // b
+        log_zr = torch.logaddexp(log_zr, part_zr.to(dtype))
+        scores, ids = _topk_merge(scores, ids, part_scores, part_ids.to(torch.int64), topk)
     distributed = group is not None and dist.is_initialized() and dist.get_world_size(group) > 1
     if distributed:
         world = dist.get_world_size(group)
@@ -217,7 +231,10 @@ def sparse_attention(q, cache, positions, block_size, topk, backend="auto", grou
     ids = ids.masked_fill(~torch.isfinite(scores), -1)
     out = torch.zeros(q.shape, dtype=dtype, device=q.device)
     lse = torch.full(shape, NEG_INF, dtype=dtype, device=q.device)
-    for start, keys, values in cache.pages(q.device, cache.touched_pages(ids, positions, b)):
+    resident = native and isinstance(cache, TensorPages) and cache.k.device == q.device
+    pieces = [(cache.offset, cache.k, cache.v)] if resident else \
+        cache.pages(q.device, cache.touched_pages(ids, positions, b))
+    for start, keys, values in pieces:
         if native:
             part, part_lse = ext.sparse_pop(qc, keys.contiguous(), values.contiguous(), pos32,
                                             ids.contiguous(), scores.float().contiguous(),

@@ -220,3 +220,32 @@ def test_model_fp32_native_matches_reference_tightly():
     for (name, pa), (_, pe) in zip(model.named_parameters(), ref.named_parameters()):
         if pa.grad is not None:
             torch.testing.assert_close(pa.grad, pe.grad, atol=1e-4, rtol=1e-3, msg=name)
+
+
+@pytest.mark.parametrize("keys,b,d,queries,topk,first", [(70000, 16, 64, 16, 64, 0), (4144, 32, 128, 5, 16, 64),
+                                                          (1000, 16, 64, 64, 200, 32), (300, 16, 64, 3, 512, 0)])
+def test_block_scores_tc_matches_reference(native, keys, b, d, queries, topk, first):
+    from exploration_b200.ops.sparse import block_scores_reference
+    torch.manual_seed(5)
+    heads = 3
+    q = torch.randn(1, queries, heads, d, device="cuda").to(torch.bfloat16)
+    k = torch.randn(1, keys, heads, d, device="cuda").to(torch.bfloat16)
+    pos = torch.randint(first, first + keys + 3 * b, (1, queries), device="cuda")
+    pos[0, 0] = -1
+    pos = pos.to(torch.int32)
+    assert native.block_scores_tc_supported(q, k, b, topk)
+    scores, ids, zr = native.block_scores_topk_tc(q, k, pos, b, first, topk)
+    ref = block_scores_reference(q.float(), k.float(), pos.long(), b, first)      # [B, Q, H, G]
+    want_zr = ref.logsumexp(-1)
+    count = min(topk, ref.shape[-1])
+    want = ref.topk(count, -1).values
+    finite = torch.isfinite(want)
+    assert torch.equal(torch.isfinite(scores), finite)
+    torch.testing.assert_close(scores[finite], want[finite], atol=2e-3, rtol=1e-4)
+    got_at_ids = ref.gather(-1, ids - first // b)
+    torch.testing.assert_close(got_at_ids[finite], scores[finite], atol=2e-3, rtol=1e-4)
+    assert torch.equal(torch.isfinite(zr), torch.isfinite(want_zr))
+    ok = torch.isfinite(want_zr)
+    torch.testing.assert_close(zr[ok], want_zr[ok], atol=2e-3, rtol=1e-4)
+    # descending order, ties by ascending block id
+    assert bool((scores[..., 1:] <= scores[..., :-1]).all())
