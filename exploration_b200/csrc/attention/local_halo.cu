@@ -316,7 +316,7 @@ std::pair<at::Tensor, at::Tensor> rope_tables(int block, int dim, const at::Devi
   // per (device, block, dim) and kept, so no host->device copy happens inside
   // a captured CUDA graph.
   static std::mutex lock;
-  static std::map<std::tuple<int, int, int>, std::pair<at::Tensor, at::Tensor>> cache;
+  static auto& cache = *new std::map<std::tuple<int, int, int>, std::pair<at::Tensor, at::Tensor>>();
   const std::lock_guard<std::mutex> guard(lock);
   const auto key = std::make_tuple(static_cast<int>(device.index()), block, dim);
   auto hit = cache.find(key);

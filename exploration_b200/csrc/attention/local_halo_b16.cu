@@ -502,7 +502,9 @@ constexpr size_t kBwdSmem = sizeof(float) * ((kRowsCta + kB) * (2 * kLdS + 2 * k
                                              2 * (kRowsCta + kB)) + (kRowsCta + kB);
 
 std::pair<at::Tensor, at::Tensor> tables(const at::Device& device) {
-  static at::Tensor cos_t[16], sin_t[16];
+  // Never destroyed (see the note on static tensors in local_tc.cu's tables).
+  static at::Tensor* cos_t = new at::Tensor[16];
+  static at::Tensor* sin_t = new at::Tensor[16];
   const int idx = device.index();
   if (!cos_t[idx].defined()) {
     auto offsets = at::arange(0, kTable, at::TensorOptions().dtype(at::kFloat));

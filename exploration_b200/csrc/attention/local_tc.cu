@@ -766,8 +766,10 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
 }
 
 std::pair<at::Tensor, at::Tensor> tc_tables(const at::Device& device) {
+  // Never destroyed: tensors must not be freed by static destructors after the
+  // CUDA allocator has shut down at process exit.
   static std::mutex lock;
-  static std::map<int, std::pair<at::Tensor, at::Tensor>> cache;
+  static auto& cache = *new std::map<int, std::pair<at::Tensor, at::Tensor>>();
   const std::lock_guard<std::mutex> guard(lock);
   auto hit = cache.find(device.index());
   if (hit != cache.end()) return hit->second;

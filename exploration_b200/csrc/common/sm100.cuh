@@ -182,6 +182,13 @@ EB_DEVICE void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
       : "r"(addr));
 }
 
+// 32 lanes x 8 consecutive 32-bit columns.
+EB_DEVICE void tmem_ld8(uint32_t addr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(addr));
+}
+
 // 32 lanes x 16 consecutive 32-bit columns.
 EB_DEVICE void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
   asm volatile(

@@ -104,6 +104,201 @@ __global__ void column_sum_kernel(const float* __restrict__ part, float* __restr
   out[c] = acc;
 }
 
+// ---------------------------------------------------------------------------
+// Register-resident LayerNorm for rows of cols = 128 * V (V float4 per lane):
+// one warp per row, the row is read once; the backward also accumulates the
+// dgamma/dbeta column partials of its CTA's rows in registers, reduces them
+// across the CTA's warps in shared memory and writes one partial row per CTA
+// (summed by one more small kernel), so x and dy are each read exactly once.
+// ---------------------------------------------------------------------------
+
+constexpr int kVecWarps = 8;
+constexpr int kVecRowsPerCta = 64;
+
+template <typename T>
+EB_DEVICE void load4(const T* p, float (&v)[4]);
+template <>
+EB_DEVICE void load4<float>(const float* p, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+template <>
+EB_DEVICE void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+template <typename T>
+EB_DEVICE void store4(T* p, const float (&v)[4]);
+template <>
+EB_DEVICE void store4<float>(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+template <>
+EB_DEVICE void store4<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[4]) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
+template <typename TIn, typename TOut, int V>
+__global__ void __launch_bounds__(kVecWarps * 32)
+ln_fwd_vec_kernel(const TIn* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                  TOut* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int rows, float eps) {
+  constexpr int cols = 128 * V;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kVecWarps + warp;
+  if (row >= rows) return;
+  const TIn* xr = x + static_cast<int64_t>(row) * cols;
+  float v[V][4];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    load4<TIn>(xr + 128 * j + 4 * lane, v[j]);
+    sum += v[j][0] + v[j][1] + v[j][2] + v[j][3];
+  }
+  const float mu = warp_sum(sum) * (1.f / cols);
+  float sq = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float d = v[j][t] - mu;
+      sq += d * d;
+    }
+  const float rs = rsqrtf(warp_sum(sq) * (1.f / cols) + eps);
+  TOut* yr = y + static_cast<int64_t>(row) * cols;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int c = 128 * j + 4 * lane;
+    const float4 ww = *reinterpret_cast<const float4*>(w + c);
+    const float4 bb = *reinterpret_cast<const float4*>(b + c);
+    float o[4] = {(v[j][0] - mu) * rs * ww.x + bb.x, (v[j][1] - mu) * rs * ww.y + bb.y,
+                  (v[j][2] - mu) * rs * ww.z + bb.z, (v[j][3] - mu) * rs * ww.w + bb.w};
+    store4<TOut>(yr + c, o);
+  }
+  if (lane == 0) {
+    mean[row] = mu;
+    rstd[row] = rs;
+  }
+}
+
+template <typename TIn, typename TGrad, int V>
+__global__ void __launch_bounds__(kVecWarps * 32)
+ln_bwd_vec_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
+                  const float* __restrict__ mean, const float* __restrict__ rstd, TIn* __restrict__ dx,
+                  float* __restrict__ part_w, float* __restrict__ part_b, int rows) {
+  constexpr int cols = 128 * V;
+  extern __shared__ float red[];                       // [kVecWarps][2][cols], then w [cols]
+  float* ws = red + kVecWarps * 2 * cols;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < cols; c += kVecWarps * 32) ws[c] = w[c];
+  __syncthreads();
+  float aw[V][4], ab[V][4];
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) aw[j][t] = ab[j][t] = 0.f;
+  const int r0 = blockIdx.x * kVecRowsPerCta;
+  const int r1 = min(rows, r0 + kVecRowsPerCta);
+  for (int row = r0 + warp; row < r1; row += kVecWarps) {
+    const int64_t base = static_cast<int64_t>(row) * cols;
+    const float mu = mean[row], rs = rstd[row];
+    float xh[V][4], dv[V][4];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      float xv[4];
+      load4<TIn>(x + base + 128 * j + 4 * lane, xv);
+      load4<TGrad>(dy + base + 128 * j + 4 * lane, dv[j]);
+      const float4 ww = *reinterpret_cast<const float4*>(ws + 128 * j + 4 * lane);
+      const float wt[4] = {ww.x, ww.y, ww.z, ww.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        xh[j][t] = (xv[t] - mu) * rs;
+        const float g = dv[j][t] * wt[t];
+        s1 += g;
+        s2 += g * xh[j][t];
+        aw[j][t] += dv[j][t] * xh[j][t];
+        ab[j][t] += dv[j][t];
+      }
+    }
+    s1 = warp_sum(s1) * (1.f / cols);
+    s2 = warp_sum(s2) * (1.f / cols);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float4 ww = *reinterpret_cast<const float4*>(ws + 128 * j + 4 * lane);
+      const float wt[4] = {ww.x, ww.y, ww.z, ww.w};
+      float o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) o[t] = rs * (dv[j][t] * wt[t] - s1 - xh[j][t] * s2);
+      store4<TIn>(dx + base + 128 * j + 4 * lane, o);
+    }
+  }
+  // CTA column partials: warps -> shared memory -> one row per CTA.
+#pragma unroll
+  for (int j = 0; j < V; ++j)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      red[(warp * 2) * cols + 128 * j + 4 * lane + t] = aw[j][t];
+      red[(warp * 2 + 1) * cols + 128 * j + 4 * lane + t] = ab[j][t];
+    }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += kVecWarps * 32) {
+    float sw = 0.f, sb = 0.f;
+#pragma unroll
+    for (int q = 0; q < kVecWarps; ++q) {
+      sw += red[(q * 2) * cols + c];
+      sb += red[(q * 2 + 1) * cols + c];
+    }
+    part_w[static_cast<int64_t>(blockIdx.x) * cols + c] = sw;
+    part_b[static_cast<int64_t>(blockIdx.x) * cols + c] = sb;
+  }
+}
+
+// out_w[c] = sum_s part_w[s][c], out_b likewise (one launch for both).
+__global__ void column_sum2_kernel(const float* __restrict__ part_w, const float* __restrict__ part_b,
+                                   float* __restrict__ out_w, float* __restrict__ out_b, int splits, int cols) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float aw = 0.f, ab = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    aw += part_w[static_cast<int64_t>(s) * cols + c];
+    ab += part_b[static_cast<int64_t>(s) * cols + c];
+  }
+  out_w[c] = aw;
+  out_b[c] = ab;
+}
+
+#define EB_DISPATCH_V(V_VALUE, NAME, ...)                                   \
+  switch (V_VALUE) {                                                        \
+    case 1: { constexpr int NAME = 1; __VA_ARGS__(); break; }              \
+    case 2: { constexpr int NAME = 2; __VA_ARGS__(); break; }              \
+    case 4: { constexpr int NAME = 4; __VA_ARGS__(); break; }              \
+    case 6: { constexpr int NAME = 6; __VA_ARGS__(); break; }              \
+    case 8: { constexpr int NAME = 8; __VA_ARGS__(); break; }              \
+    case 12: { constexpr int NAME = 12; __VA_ARGS__(); break; }            \
+    case 16: { constexpr int NAME = 16; __VA_ARGS__(); break; }            \
+    default: TORCH_CHECK(false, "unsupported LayerNorm width");            \
+  }
+
+#define EB_DISPATCH_V_SMALL(V_VALUE, NAME, ...)                             \
+  switch (V_VALUE) {                                                        \
+    case 1: { constexpr int NAME = 1; __VA_ARGS__(); break; }              \
+    case 2: { constexpr int NAME = 2; __VA_ARGS__(); break; }              \
+    case 4: { constexpr int NAME = 4; __VA_ARGS__(); break; }              \
+    case 6: { constexpr int NAME = 6; __VA_ARGS__(); break; }              \
+    case 8: { constexpr int NAME = 8; __VA_ARGS__(); break; }              \
+    default: TORCH_CHECK(false, "unsupported LayerNorm width");            \
+  }
+
+bool vec_width(int cols) {
+  if (cols % 128) return false;
+  const int v = cols / 128;
+  return v == 1 || v == 2 || v == 4 || v == 6 || v == 8 || v == 12 || v == 16;
+}
+
 EB_DEVICE float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 
 EB_DEVICE float gelu_grad(float v) {
@@ -171,6 +366,21 @@ std::vector<at::Tensor> layer_norm_fwd(const at::Tensor& x, const at::Tensor& w,
   if (rows == 0) return {y, mean, rstd};
   auto stream = at::cuda::getCurrentCUDAStream();
   const int grid = cdiv(rows, kRowWarps);
+  if (vec_width(cols)) {
+    EB_DISPATCH_FLOAT_BF16(x.scalar_type(), TIn, [&] {
+      EB_DISPATCH_FLOAT_BF16(out_dtype, TOut, [&] {
+        EB_DISPATCH_V(cols / 128, V, [&] {
+          ln_fwd_vec_kernel<TIn, TOut, V><<<cdiv(rows, kVecWarps), kVecWarps * 32, 0, stream>>>(
+              reinterpret_cast<const TIn*>(x.data_ptr()), w.data_ptr<float>(), b.data_ptr<float>(),
+              reinterpret_cast<TOut*>(y.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows,
+              static_cast<float>(eps));
+        });
+      });
+    });
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch(1);
+    return {y, mean, rstd};
+  }
   EB_DISPATCH_FLOAT_BF16(x.scalar_type(), TIn, [&] {
     EB_DISPATCH_FLOAT_BF16(out_dtype, TOut, [&] {
       layer_norm_fwd_kernel<TIn, TOut><<<grid, kRowWarps * 32, 0, stream>>>(
@@ -194,6 +404,29 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
   auto db = at::zeros({cols}, x.options().dtype(at::kFloat));
   if (rows == 0) return {dx, dw, db};
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (vec_width(cols) && cols <= 1024) {
+    const int ctas = cdiv(rows, kVecRowsPerCta);
+    auto pw = at::empty({ctas, cols}, x.options().dtype(at::kFloat));
+    auto pb = at::empty({ctas, cols}, x.options().dtype(at::kFloat));
+    const size_t smem = sizeof(float) * (kVecWarps * 2 + 1) * cols;
+    EB_DISPATCH_FLOAT_BF16(x.scalar_type(), TIn, [&] {
+      EB_DISPATCH_FLOAT_BF16(dy.scalar_type(), TGrad, [&] {
+        EB_DISPATCH_V_SMALL(cols / 128, V, [&] {
+          auto kernel = ln_bwd_vec_kernel<TIn, TGrad, V>;
+          EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+          kernel<<<ctas, kVecWarps * 32, smem, stream>>>(
+              reinterpret_cast<const TGrad*>(dy.data_ptr()), reinterpret_cast<const TIn*>(x.data_ptr()),
+              w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+              reinterpret_cast<TIn*>(dx.data_ptr()), pw.data_ptr<float>(), pb.data_ptr<float>(), rows);
+        });
+      });
+    });
+    column_sum2_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(pw.data_ptr<float>(), pb.data_ptr<float>(),
+                                                           dw.data_ptr<float>(), db.data_ptr<float>(), ctas, cols);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch(2);
+    return {dx, dw, db};
+  }
   const int splits = row_splits(rows);
   const int per_split = cdiv(rows, splits);
   auto part_w = at::empty({splits, cols}, x.options().dtype(at::kFloat));

@@ -35,7 +35,7 @@ using namespace sm100;
 
 constexpr int kTile = 128;
 constexpr int kStages = 4;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;   // warps 0-3: TMA, MMA, TMEM owner, idle; 4-11: epilogue
 
 struct ScoreArgs {
   const int* pos;        // [B, Q] (this call's query rows)
@@ -56,12 +56,6 @@ struct alignas(1024) ScoreSmem {
   int abort;
   int pos[N];
 };
-
-EB_DEVICE float lse_add(float a, float b) {
-  const float m = fmaxf(a, b);
-  if (m == kNegInf) return kNegInf;
-  return m + logf(expf(a - m) + expf(b - m));
-}
 
 template <int D, int N, int B>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -85,7 +79,7 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 128);
+      mbar_init(&sm.acc_empty[s], 256);
     }
     sm.abort = 0;
     fence_barrier_init();
@@ -141,15 +135,19 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
       }
     }
   } else if (warp >= 4) {
-    const int w = warp - 4;
+    constexpr int kHalf = N / 2;                      // query columns per warpgroup
+    const int ew = warp - 4, grp = ew >> 2, w = ew & 3;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
-    // Running log-sum-exp of this CTA's visible blocks per query, one slot per
-    // block-owner lane (lane % B == 0) in shared memory.
-    constexpr int kOwners = 32 / B;
-    __shared__ float zacc[4][kOwners][N];
-    const int slot = lane / B;
-    for (int c = lane; c < kOwners * N; c += 32) zacc[w][c / N][c % N] = kNegInf;
-    __syncwarp();
+    const float scale2 = a.scale * 1.4426950408889634f;
+    // Running base-2 (max, sum) of this CTA's visible block scores per query;
+    // only block-owner lanes (lane % B == 0) accumulate.
+    float zm[kHalf], zs[kHalf];
+#pragma unroll
+    for (int c = 0; c < kHalf; ++c) {
+      zm[c] = kNegInf;
+      zs[c] = 0.f;
+    }
+    const bool owner = (lane % B) == 0;
     for (int i = 0; i < count; ++i) {
       const int buf = i & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.acc_full[buf], (i >> 1) & 1, abort, a.err, kSiteSFull))) break;
@@ -159,41 +157,68 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
       const int g = key / B;                                 // gate block within this call
       const bool full = (g + 1) * B <= a.keys;
       const int64_t gid = (a.first + static_cast<int64_t>(g) * B) / B;
-      const bool owner = (lane % B) == 0;
+      uint32_t r[kHalf];
+      if constexpr (kHalf == 8) {
+        uint32_t (&r8)[8] = reinterpret_cast<uint32_t(&)[8]>(r);
+        tmem_ld8(lane_addr + buf * N + grp * kHalf, r8);
+      } else {
+        uint32_t (&r16)[16] = reinterpret_cast<uint32_t(&)[16]>(r);
+        tmem_ld16(lane_addr + buf * N + grp * kHalf, r16);
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sm.acc_empty[buf]);                        // the values are in registers
 #pragma unroll
-      for (int c0 = 0; c0 < N; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(lane_addr + buf * N + c0, r);
-        tc_wait_ld();
+      for (int j = 0; j < kHalf; ++j) {
+        const int c = grp * kHalf + j;
+        const float x = key < a.keys ? __uint_as_float(r[j]) * scale2 : kNegInf;
+        float m = x;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int c = c0 + j;
-          const float x = key < a.keys ? __uint_as_float(r[j]) * a.scale : kNegInf;
-          float m = x;
+        for (int o = 1; o < B; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float e = m == kNegInf ? 0.f : ex2(x - m);
 #pragma unroll
-          for (int o = 1; o < B; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          float e = m == kNegInf ? 0.f : expf(x - m);
-#pragma unroll
-          for (int o = 1; o < B; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
-          const int p = sm.pos[c];
-          const bool visible = full && p >= 0 && gid < p / B - 1 && c < a.queries;
-          const float sb = visible && m != kNegInf ? m + logf(e) : kNegInf;
-          if (owner && c < a.queries && g < a.groups) {
-            a.scores[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.groups + g] = sb;
-            zacc[w][slot][c] = lse_add(zacc[w][slot][c], sb);
+        for (int o = 1; o < B; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+        const int p = sm.pos[c];
+        const bool visible = full && p >= 0 && gid < p / B - 1 && c < a.queries && m != kNegInf;
+        if (owner && c < a.queries && g < a.groups) {
+          const float sb2 = visible ? m + lg2(e) : kNegInf;
+          a.scores[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.groups + g] =
+              visible ? sb2 * 0.6931471805599453f : kNegInf;
+          if (visible) {
+            if (sb2 > zm[j]) {
+              zs[j] = zs[j] * ex2(zm[j] - sb2) + 1.f;
+              zm[j] = sb2;
+            } else {
+              zs[j] += ex2(sb2 - zm[j]);
+            }
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.acc_empty[buf]);
     }
-    // Combine the owners' running sums (all slots of the four warps).
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    for (int c = threadIdx.x - 128; c < a.queries; c += 128) {
-      float v = kNegInf;
-      for (int ww = 0; ww < 4; ++ww)
-        for (int o = 0; o < kOwners; ++o) v = lse_add(v, zacc[ww][o][c]);
-      a.zr_part[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.ctas + blockIdx.x] = v;
+    // Combine owners and warps: per query, the (max, sum) pairs of up to
+    // 4 warps x (32 / B) owners of this warpgroup.
+    constexpr int kOwners = 32 / B;
+    __shared__ float zpart[2][4 * kOwners][kHalf][2];
+    if (owner) {
+#pragma unroll
+      for (int j = 0; j < kHalf; ++j) {
+        zpart[grp][w * kOwners + lane / B][j][0] = zm[j];
+        zpart[grp][w * kOwners + lane / B][j][1] = zs[j];
+      }
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const int t = threadIdx.x - 128;
+    if (t < N) {
+      const int gg = t / kHalf, j = t % kHalf;
+      float m = kNegInf;
+      for (int o = 0; o < 4 * kOwners; ++o) m = fmaxf(m, zpart[gg][o][j][0]);
+      float sum = 0.f;
+      if (m != kNegInf)
+        for (int o = 0; o < 4 * kOwners; ++o)
+          if (zpart[gg][o][j][0] != kNegInf) sum += zpart[gg][o][j][1] * ex2(zpart[gg][o][j][0] - m);
+      if (t < a.queries)
+        a.zr_part[((static_cast<int64_t>(batch) * a.queries + t) * a.heads + head) * a.ctas + blockIdx.x] =
+            m == kNegInf ? kNegInf : (m + lg2(sum)) * 0.6931471805599453f;
     }
   }
   tc_fence_before();
@@ -216,38 +241,32 @@ EB_DEVICE uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Top-k of one segment of `len` values (row `blockIdx.y`, segment `blockIdx.x`
+// of `seg_len`): radix select of the k-th largest order key, then the winners
+// sorted by (score desc, index asc). `idx_in` (nullable) maps positions to
+// the indices used for ties and output; candidates beyond `len` are padding.
 __global__ void __launch_bounds__(kSelThreads)
-topk_select_kernel(const float* __restrict__ scores, int groups, int k, const float* __restrict__ zr_part, int ctas,
-                   float* __restrict__ out_scores, int64_t* __restrict__ out_ids, float* __restrict__ zr_out,
-                   int64_t id_base) {
+topk_select_kernel(const float* __restrict__ values, const int* __restrict__ idx_in, int row_len, int seg_len, int k,
+                   float* __restrict__ out_v, int* __restrict__ out_i, int64_t* __restrict__ out_ids, int64_t id_base) {
   __shared__ uint32_t hist[256];
-  __shared__ uint32_t sel_prefix, sel_remaining;
-  __shared__ int n_gt, n_eq;
+  __shared__ uint32_t sel_prefix;
+  __shared__ int sel_remaining, n_gt;
   __shared__ float cand_v[kMaxK];
   __shared__ int cand_i[kMaxK];
-  const int64_t row = blockIdx.x;
-  const float* x = scores + row * groups;
+  const int64_t row = blockIdx.y;
+  const int seg = blockIdx.x, segs = gridDim.x;
+  const int lo = seg * seg_len;
+  const int len = max(0, min(seg_len, row_len - lo));
+  const float* x = values + row * row_len + lo;
+  const int* ix = idx_in != nullptr ? idx_in + row * row_len + lo : nullptr;
   const int tid = threadIdx.x;
-  // log Z_R of the row from the CTA parts.
-  if (tid < 32) {
-    float m = kNegInf;
-    for (int i = tid; i < ctas; i += 32) m = fmaxf(m, zr_part[row * ctas + i]);
-    m = warp_max(m);
-    float s = 0.f;
-    for (int i = tid; i < ctas; i += 32) {
-      const float v = zr_part[row * ctas + i];
-      s += v == kNegInf ? 0.f : expf(v - m);
-    }
-    s = warp_sum(s);
-    if (tid == 0) zr_out[row] = (m == kNegInf || s <= 0.f) ? kNegInf : m + logf(s);
-  }
-  // Radix select of the k-th largest order key, 8 bits per pass from the top.
+  const int kk = min(k, len);
   uint32_t prefix = 0, mask = 0;
-  int remaining = k;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  int remaining = kk;
+  for (int shift = 24; shift >= 0 && kk > 0; shift -= 8) {
     for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < groups; i += kSelThreads) {
+    for (int i = tid; i < len; i += kSelThreads) {
       const uint32_t key = order_key(x[i]);
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
@@ -267,45 +286,37 @@ topk_select_kernel(const float* __restrict__ scores, int groups, int k, const fl
     mask |= 255u << shift;
     __syncthreads();
   }
-  // prefix is the exact order key of the k-th largest value; `remaining` of
-  // the elements equal to it are taken (lowest block ids first).
-  if (tid == 0) {
-    n_gt = 0;
-    n_eq = 0;
-  }
+  if (tid == 0) n_gt = 0;
   __syncthreads();
   const int take_eq = remaining;
-  const int gt_total = k - take_eq;
-  for (int i = tid; i < groups; i += kSelThreads) {
+  const int gt_total = kk - take_eq;
+  for (int i = tid; i < len && kk > 0; i += kSelThreads) {
     const uint32_t key = order_key(x[i]);
     if (key > prefix) {
       const int slot = atomicAdd(&n_gt, 1);
       cand_v[slot] = x[i];
-      cand_i[slot] = i;
+      cand_i[slot] = ix != nullptr ? ix[i] : lo + i;
     }
   }
   __syncthreads();
-  // Equal keys: in ascending index order, one warp scanning the row.
-  if (tid < 32) {
+  if (tid < 32 && kk > 0) {   // ties at the threshold: lowest positions first
     int taken = 0;
-    for (int base = 0; base < groups && taken < take_eq; base += 32) {
+    for (int base = 0; base < len && taken < take_eq; base += 32) {
       const int i = base + tid;
-      const bool eq = i < groups && order_key(x[i]) == prefix;
+      const bool eq = i < len && order_key(x[i]) == prefix;
       const unsigned ballot = __ballot_sync(0xffffffffu, eq);
       const int before = __popc(ballot & ((1u << tid) - 1u));
       if (eq && taken + before < take_eq) {
         cand_v[gt_total + taken + before] = x[i];
-        cand_i[gt_total + taken + before] = i;
+        cand_i[gt_total + taken + before] = ix != nullptr ? ix[i] : lo + i;
       }
       taken += __popc(ballot);
     }
   }
   __syncthreads();
-  // Bitonic sort of the k candidates (padded to a power of two): descending
-  // score, ascending block id on ties.
   int n2 = 1;
   while (n2 < k) n2 <<= 1;
-  for (int i = k + tid; i < n2; i += kSelThreads) {
+  for (int i = kk + tid; i < n2; i += kSelThreads) {
     cand_v[i] = kNegInf;
     cand_i[i] = 0x7fffffff;
   }
@@ -330,10 +341,29 @@ topk_select_kernel(const float* __restrict__ scores, int groups, int k, const fl
       __syncthreads();
     }
   }
+  const int64_t out_base = (row * segs + seg) * static_cast<int64_t>(k);
   for (int i = tid; i < k; i += kSelThreads) {
-    out_scores[row * k + i] = cand_v[i];
-    out_ids[row * k + i] = id_base + cand_i[i];
+    if (out_v != nullptr) out_v[out_base + i] = cand_v[i];
+    if (out_i != nullptr) out_i[out_base + i] = cand_i[i];
+    if (out_ids != nullptr) out_ids[out_base + i] = id_base + cand_i[i];
   }
+}
+
+// log Z_R of each row from the scoring CTAs' parts (natural-log units).
+__global__ void zr_combine_kernel(const float* __restrict__ zr_part, int ctas, int rows, float* __restrict__ zr) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float m = kNegInf;
+  for (int i = lane; i < ctas; i += 32) m = fmaxf(m, zr_part[static_cast<int64_t>(row) * ctas + i]);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int i = lane; i < ctas; i += 32) {
+    const float v = zr_part[static_cast<int64_t>(row) * ctas + i];
+    s += v == kNegInf ? 0.f : expf(v - m);
+  }
+  s = warp_sum(s);
+  if (lane == 0) zr[row] = (m == kNegInf || s <= 0.f) ? kNegInf : m + logf(s);
 }
 
 template <int D, int N, int B>
@@ -359,8 +389,7 @@ void dispatch_n(const at::Tensor& q, const at::Tensor& k, ScoreArgs& args, int b
                 cudaStream_t stream) {
   const int n = q.size(1);
   if (n <= 16) dispatch_block<D, 16>(q, k, args, batch, heads, block, stream);
-  else if (n <= 32) dispatch_block<D, 32>(q, k, args, batch, heads, block, stream);
-  else dispatch_block<D, 64>(q, k, args, batch, heads, block, stream);
+  else dispatch_block<D, 32>(q, k, args, batch, heads, block, stream);
 }
 
 }  // namespace
@@ -368,7 +397,7 @@ void dispatch_n(const at::Tensor& q, const at::Tensor& k, ScoreArgs& args, int b
 bool block_scores_tc_supported(const at::Tensor& q, const at::Tensor& k, int64_t block, int64_t topk) {
   const int64_t d = q.size(3);
   return q.is_cuda() && q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && q.is_contiguous() &&
-         k.is_contiguous() && (d == 64 || d == 128) && (block == 16 || block == 32) && q.size(1) <= 64 &&
+         k.is_contiguous() && (d == 64 || d == 128) && (block == 16 || block == 32) && q.size(1) <= 32 &&
          topk >= 1 && topk <= kMaxK;
 }
 
@@ -405,11 +434,27 @@ std::vector<at::Tensor> block_scores_topk_tc(const at::Tensor& q, const at::Tens
   auto ids = at::empty({batch, queries, heads, kk}, q.options().dtype(at::kLong));
   auto zr = at::empty({batch, queries, heads}, fopt);
   const int rows = batch * queries * heads;
-  topk_select_kernel<<<rows, kSelThreads, 0, stream>>>(scores.data_ptr<float>(), groups, static_cast<int>(kk),
-                                                        zr_part.data_ptr<float>(), ctas, top.data_ptr<float>(),
-                                                        ids.data_ptr<int64_t>(), zr.data_ptr<float>(), first / block);
+  // Stage 1: top-kk of each segment of kSegLen block scores; stage 2: of the candidates.
+  constexpr int kSegLen = 4096;
+  const int segs = (groups + kSegLen - 1) / kSegLen;
+  if (segs == 1) {
+    topk_select_kernel<<<dim3(1, rows), kSelThreads, 0, stream>>>(scores.data_ptr<float>(), nullptr, groups, groups,
+                                                                   static_cast<int>(kk), top.data_ptr<float>(), nullptr,
+                                                                   ids.data_ptr<int64_t>(), first / block);
+  } else {
+    auto cand_v = at::empty({rows, segs, kk}, fopt);
+    auto cand_i = at::empty({rows, segs, kk}, q.options().dtype(at::kInt));
+    topk_select_kernel<<<dim3(segs, rows), kSelThreads, 0, stream>>>(
+        scores.data_ptr<float>(), nullptr, groups, kSegLen, static_cast<int>(kk), cand_v.data_ptr<float>(),
+        cand_i.data_ptr<int>(), nullptr, 0);
+    const int cand_len = static_cast<int>(segs * kk);
+    topk_select_kernel<<<dim3(1, rows), kSelThreads, 0, stream>>>(
+        cand_v.data_ptr<float>(), cand_i.data_ptr<int>(), cand_len, cand_len, static_cast<int>(kk),
+        top.data_ptr<float>(), nullptr, ids.data_ptr<int64_t>(), first / block);
+  }
+  zr_combine_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(zr_part.data_ptr<float>(), ctas, rows, zr.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  count_launch(2);
+  count_launch(segs == 1 ? 3 : 4);
   return {top, ids, zr};
 }
 

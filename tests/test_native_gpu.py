@@ -105,12 +105,13 @@ def test_local_attention_matches_reference(n, b, d, prev, dtype):
         torch.testing.assert_close(a.double(), e, atol=atol * 4, rtol=rtol)
 
 
+@pytest.mark.parametrize("cols,rows", [(1000, 300), (1024, 517), (768, 64), (128, 3), (1536, 200)])
 @pytest.mark.parametrize("dtype,out", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
                                        (torch.bfloat16, torch.bfloat16)])
-def test_layer_norm(dtype, out, native):
+def test_layer_norm(dtype, out, cols, rows, native):
     torch.manual_seed(0)
-    x = torch.randn(300, 1000, device="cuda", dtype=dtype) * 3 + 1
-    norm = torch.nn.LayerNorm(1000).cuda()
+    x = torch.randn(rows, cols, device="cuda", dtype=dtype) * 3 + 1
+    norm = torch.nn.LayerNorm(cols).cuda()
     torch.nn.init.normal_(norm.weight)
     torch.nn.init.normal_(norm.bias)
     xr = x.detach().float().requires_grad_()
@@ -118,7 +119,7 @@ def test_layer_norm(dtype, out, native):
     with torch.autocast("cuda", dtype=torch.bfloat16, enabled=out == torch.bfloat16):
         y = fused.layer_norm(xn, norm, "cuda")
     assert y.dtype == out
-    ref = torch.nn.functional.layer_norm(xr, (1000,), norm.weight, norm.bias, norm.eps)
+    ref = torch.nn.functional.layer_norm(xr, (cols,), norm.weight, norm.bias, norm.eps)
     atol = 2e-5 if out == torch.float32 and dtype == torch.float32 else 3e-2
     torch.testing.assert_close(y.float(), ref, atol=atol, rtol=1e-2)
     g = torch.randn_like(ref)
@@ -223,7 +224,7 @@ def test_model_fp32_native_matches_reference_tightly():
 
 
 @pytest.mark.parametrize("keys,b,d,queries,topk,first", [(70000, 16, 64, 16, 64, 0), (4144, 32, 128, 5, 16, 64),
-                                                          (1000, 16, 64, 64, 200, 32), (300, 16, 64, 3, 512, 0)])
+                                                          (1000, 16, 64, 32, 200, 32), (300, 16, 64, 3, 512, 0), (200000, 32, 64, 16, 64, 0)])
 def test_block_scores_tc_matches_reference(native, keys, b, d, queries, topk, first):
     from exploration_b200.ops.sparse import block_scores_reference
     torch.manual_seed(5)
