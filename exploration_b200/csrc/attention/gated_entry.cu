@@ -8,6 +8,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "gated_common.cuh"
 #include "../common/tma.cuh"
 
@@ -46,6 +49,10 @@ void gated_bwd_simt_launch(const at::Tensor& grad, const at::Tensor& q, const at
                            const at::Tensor& pr, const at::Tensor& zr, const at::Tensor& lse, int64_t block,
                            at::Tensor& dq, at::Tensor& dk, at::Tensor& dv);
 bool gated_tc_supported(const at::Tensor& q, int64_t block);
+bool gated_tc2_supported(const at::Tensor& q, int64_t block);
+void gated_fwd_tc2_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& pos,
+                          int64_t block, at::Tensor& out, at::Tensor& rc, at::Tensor& pr, at::Tensor& zr,
+                          at::Tensor& lse);
 void gated_fwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& pos,
                          int64_t block, at::Tensor& out, at::Tensor& rc, at::Tensor& pr, at::Tensor& zr,
                          at::Tensor& lse);
@@ -85,7 +92,12 @@ std::vector<at::Tensor> gated_attention_fwd(const at::Tensor& q, const at::Tenso
   auto zr = at::empty_like(pr);
   auto lse = at::empty_like(pr);
   if (q.numel() == 0) return {out, rc, pr, zr, lse};
-  if (gated_tc_supported(q, block))
+  // Two query tiles per CTA for head dim 64 unless EB200_GATED_FWD=single (A/B comparisons).
+  const char* choice = std::getenv("EB200_GATED_FWD");
+  const bool single = choice != nullptr && std::string(choice) == "single";
+  if (!single && gated_tc2_supported(q, block))
+    gated_fwd_tc2_launch(q, k, v, pos, block, out, rc, pr, zr, lse);
+  else if (gated_tc_supported(q, block))
     gated_fwd_tc_launch(q, k, v, pos, block, out, rc, pr, zr, lse);
   else
     gated_fwd_simt_launch(q, k, v, pos, block, out, rc, pr, zr, lse);
