@@ -25,6 +25,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 
@@ -865,21 +867,36 @@ std::vector<at::Tensor> local_tc_bwd(const at::Tensor& dout, const at::Tensor& q
                  device_error_slot(qkv.device().index())};
   auto stream = at::cuda::getCurrentCUDAStream();
   const int ctas = (n + kM - 1) / kM;
+  // EB200_DEBUG_LOCAL=1: synchronise and report after every step (diagnostics).
+  static const bool debug = std::getenv("EB200_DEBUG_LOCAL") != nullptr;
+  auto trace = [&](const char* what) {
+    if (!debug) return;
+    const cudaError_t e = cudaStreamSynchronize(stream);
+    std::fprintf(stderr, "[local_tc_bwd] %s: %s (n=%lld B=%d H=%d qkv=%p dout=%p out=%p lse=%p dqkv=%p)\n", what,
+                 cudaGetErrorString(e), static_cast<long long>(n), batch, heads, qkv.data_ptr(), dout.data_ptr(),
+                 out.data_ptr(), lse.data_ptr(), dqkv.data_ptr());
+    std::fflush(stderr);
+  };
+  trace("start");
   {
     const size_t smem = std::max<size_t>(sizeof(LtDqSmem) + 1024, 80 * 1024);
     auto kernel = local_tc_dq_kernel;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    trace("dq attribute");
     kernel<<<dim3(ctas, heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout, args);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    trace("dq kernel");
   }
   {
     // One CTA per SM: the kernel holds all 512 TMEM columns.
     const size_t smem = std::max<size_t>(sizeof(LtDkvSmem) + 1024, 120 * 1024);
     auto kernel = local_tc_dkv_kernel;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    trace("dkv attribute");
     kernel<<<dim3(ctas + (has_prev ? 1 : 0), heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout,
                                                                                        t_dout16, args, ctas);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    trace("dkv kernel");
   }
   count_launch(2);
   return {dqkv, dprev};
