@@ -126,11 +126,16 @@ class _LayerNormNative(torch.autograd.Function):
         return dx.view(ctx.shape), dw, db, None, None
 
 
+def _fp32(t):
+    return t if t is None or t.dtype == torch.float32 else t.float()
+
+
 def layer_norm(x, norm: torch.nn.LayerNorm, backend: str = "auto"):
     """``norm(x)``; on CUDA the output is already in the matmul dtype."""
     cdt = compute_dtype(x, norm.weight.dtype)
     if use_native(x, backend, cdt) and x.dtype in (torch.float32, torch.bfloat16):
-        return _LayerNormNative.apply(x, norm.weight, norm.bias, norm.eps, cdt)
+        # The kernels read fp32 affine parameters (a bf16-cast model passes copies).
+        return _LayerNormNative.apply(x, _fp32(norm.weight), _fp32(norm.bias), norm.eps, cdt)
     return F.layer_norm(x, norm.normalized_shape, norm.weight, norm.bias, norm.eps)
 
 
@@ -158,7 +163,7 @@ def linear_residual(x, layer: torch.nn.Linear, residual, backend: str = "auto"):
     cdt = compute_dtype(x, layer.weight.dtype)
     if use_native(x, backend, cdt) and cdt == torch.bfloat16 and residual.dtype == torch.float32 \
             and gemm.usable(x.to(cdt), layer):
-        return gemm.LinearResidual.apply(x.to(cdt), layer.weight, layer.bias, residual)
+        return gemm.LinearResidual.apply(x.to(cdt), layer.weight, _fp32(layer.bias), residual)
     return residual + linear(x, layer, backend)
 
 
@@ -168,7 +173,7 @@ def ffn_residual(h, y, ffn: torch.nn.Sequential, backend: str = "auto"):
     cdt = compute_dtype(h, up.weight.dtype)
     if use_native(h, backend, cdt) and cdt == torch.bfloat16 and y.dtype == torch.float32 \
             and gemm.usable(h.to(cdt), up, down):
-        return gemm.FFNResidual.apply(h.to(cdt), y, up.weight, up.bias, down.weight, down.bias)
+        return gemm.FFNResidual.apply(h.to(cdt), y, up.weight, _fp32(up.bias), down.weight, _fp32(down.bias))
     return y + feed_forward(h, ffn, backend)
 
 
@@ -198,7 +203,7 @@ def feed_forward(x, ffn: torch.nn.Sequential, backend: str = "auto"):
     if use_native(x, backend, cdt):
         w1 = cast_param(up.weight, cdt)
         h = torch.matmul(x.to(cdt), w1.t())
-        u = _BiasGeluNative.apply(h, up.bias)
+        u = _BiasGeluNative.apply(h, _fp32(up.bias))
         return F.linear(u, cast_param(down.weight, cdt), cast_param(down.bias, cdt))
     return down(act(up(x)))
 

@@ -143,7 +143,8 @@ class UlyssesFused:
 
     def heads_to_linear_residual(self, heads, layer, residual):
         """``residual + to_sequence(heads) W^T + b`` (fp32) for this rank's shard."""
-        return _HeadsToLinearResidual.apply(heads, layer.weight, layer.bias, residual, self)
+        bias = layer.bias if layer.bias is None or layer.bias.dtype == torch.float32 else layer.bias.float()
+        return _HeadsToLinearResidual.apply(heads, layer.weight, bias, residual, self)
 
     # Generic exchanges (no projection to fuse with) stay on the collective path.
     def to_heads(self, x):

@@ -264,3 +264,26 @@ def test_gated_forward_two_tile_kernel_matches_single(n, b, monkeypatch):
         monkeypatch.setenv("EB200_GATED_FWD", "single")
         one = dense_attention(q, k, v, pos, b, "cuda")
     torch.testing.assert_close(two.float(), one.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("tier", ["cuda", "cpu"])
+def test_bf16_cast_model_inference_native(tier, tmp_path):
+    """Evaluation casts the model to bf16 (norm/bias parameters included); the
+    native inference path must accept it and agree with the fp32 model."""
+    from exploration_b200 import ExecutionConfig, build_model
+    from exploration_b200.runtime.inference import InferenceSession
+    torch.manual_seed(11)
+    options = {"model": "stack", "vocab_size": 128, "dim": 256, "heads": 4, "block_size": 16, "topk": 8,
+               "arch": "Lx2,G", "ffn_ratio": 4.0}
+    model = build_model(options, execution=ExecutionConfig(backend="cuda"), device="cuda").eval()
+    ids = torch.randint(128, (1, 3000))
+    pos = torch.tensor([[100, 1500, 2999]])
+    mask = torch.zeros_like(ids, dtype=torch.bool).scatter_(1, pos, True)
+    with torch.no_grad():
+        expected = model(ids.cuda(), sup=mask.cuda(), compact=True).float()
+        model.to(torch.bfloat16)
+        with InferenceSession(model, cache=tier, cache_dir=str(tmp_path), page_tokens=1024) as session:
+            session.prefill(ids, pos)
+            actual = torch.cat([logits for _, logits, _ in session.iter_logits()], 1).float()
+    assert torch.isfinite(actual).all()
+    torch.testing.assert_close(actual.cpu(), expected.cpu(), atol=0.3, rtol=0.1)
