@@ -25,9 +25,20 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// The tensor-map encoder is a driver entry point: it needs a CUDA context
+// current on the calling thread. A fresh thread (the autograd engine's device
+// thread running a backward as its first CUDA work) may not have one yet, so
+// bind the current device's primary context explicitly before encoding.
+inline void bind_primary_context() {
+  int device = 0;
+  cudaGetDevice(&device);
+  cudaSetDevice(device);
+}
+
 // bf16 tensor [B, L, H, D] viewed as (D, H, L, B); boxes of 64 x 1 x rows x 1
 // with 128-byte swizzle (the canonical K-major / MN-major UMMA atom).
 inline CUtensorMap make_bhld_map(void* base, int batch, int length, int heads, int dim, int rows) {
+  bind_primary_context();
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   CUtensorMap map;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(heads),
@@ -47,6 +58,7 @@ inline CUtensorMap make_bhld_map(void* base, int batch, int length, int heads, i
 // 64 columns x box_rows rows, 128-byte swizzle.
 inline CUtensorMap make_matrix_map(const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
                                    int box_rows) {
+  bind_primary_context();
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   CUtensorMap map;
@@ -65,6 +77,7 @@ inline CUtensorMap make_matrix_map(const void* base, int64_t rows, int64_t cols,
 // 64 columns x box_rows rows x 1 plane, 128-byte swizzle. `base` may be a
 // peer GPU's memory mapped into this process (plain tiled loads only).
 inline CUtensorMap make_plane_map(const void* base, int64_t planes, int64_t rows, int64_t cols, int box_rows) {
+  bind_primary_context();
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((cols * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   CUtensorMap map;

@@ -33,6 +33,8 @@ from ..ops.sparse import TensorPages, sparse_attention
 from .faults import maybe_fail
 from .memory import plan_inference
 
+NATIVE_PREFILL_CHUNK = 16384   # prefill chunk (tokens) on the native CUDA path
+
 
 def _allocate_file(path: Path, size: int) -> None:
     with open(path, "xb") as handle:
@@ -214,8 +216,13 @@ class InferenceSession:
                                  self.plan, start, self.options["cache_dir"])
             self.query_states = self._query_storage(batch, positions.shape[1],
                                                     positions.numel() * m.dim * element)
-            for lo in range(warm, end, self.plan.encoder_chunk):
-                hi = min(end, lo + self.plan.encoder_chunk)
+            step = self.plan.encoder_chunk
+            if self.device.type == "cuda" and getattr(m, "backend", "auto") != "torch":
+                # Values do not depend on the chunk; on the native path bigger
+                # chunks mean far fewer launches (the workspace holds them).
+                step = max(step, NATIVE_PREFILL_CHUNK // b * b)
+            for lo in range(warm, end, step):
+                hi = min(end, lo + step)
                 maybe_fail("prefill_chunk")
                 x = m.embedding(input_ids[:, lo:hi].to(self.device, non_blocking=True))
                 for i, layer in enumerate(m.local):

@@ -287,3 +287,23 @@ def test_bf16_cast_model_inference_native(tier, tmp_path):
             actual = torch.cat([logits for _, logits, _ in session.iter_logits()], 1).float()
     assert torch.isfinite(actual).all()
     torch.testing.assert_close(actual.cpu(), expected.cpu(), atol=0.3, rtol=0.1)
+
+
+def test_native_backward_as_first_cuda_work_of_the_autograd_thread():
+    """A fresh process whose first backward node is a native op: the autograd
+    engine's device thread has no CUDA context yet when the op encodes its TMA
+    tensor maps (which needs one). Runs in a subprocess so the thread is new."""
+    import subprocess
+    import sys
+    code = (
+        "import torch\n"
+        "from exploration_b200.ops import fused\n"
+        "qkv = torch.randn(1, 1024, 3, 16, 64, device='cuda').to(torch.bfloat16).requires_grad_()\n"
+        "out = fused.local_attention(qkv, None, 0, 0, 1024, 16, 16, 'cuda')\n"
+        "out.backward(torch.randn_like(out))\n"
+        "torch.cuda.synchronize()\n"
+        "print('ok', float(qkv.grad.float().abs().sum()) > 0)\n")
+    for _ in range(3):
+        proc = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+        assert proc.returncode == 0, proc.stderr[-2000:]
+        assert "ok True" in proc.stdout
