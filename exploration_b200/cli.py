@@ -61,6 +61,8 @@ OPTIONS = [
     ("--activation-offload", TRAIN, dict(action="store_true",
                                          help="offload autograd saved tensors to pinned host RAM")),
     ("--optimizer-shard", TRAIN, dict(action=BOOL, default=True)),
+    ("--profile", TRAIN, dict(default="", help="directory for a torch.profiler trace of steps 2-4 "
+                                                "(NVTX phase ranges included); empty disables")),
     ("--cuda-graph", TRAIN, dict(dest="cuda_graph", action=BOOL, default=False,
                                  help="capture each training step in a CUDA graph (flat AdamW, "
                                       "explicit gradient reduction; CUDA, one micro-step)")),

@@ -37,6 +37,7 @@ from ..config import canonical_backend
 from ..ops import fused
 from ..ops.attention import dense_attention
 from ..parallel.context import ParallelContext
+from ..runtime import trace
 from .blocks import FeedForward, HaloMemoryBlock, KVProjection, RotaryEmbedding, _gather_heads
 
 # On the native path one query tile covers this many supervised positions:
@@ -275,7 +276,8 @@ class StackModel(nn.Module):
             safe = order.clamp_max(n - 1)
             pos = torch.where(valid, order + offset, -1)
             picked = targets.gather(1, safe).masked_fill(~valid, -100)
-        x, k, v = self.encode_shard(input_ids, parallel, offset)
+        with trace.phase("encode"):
+            x, k, v = self.encode_shard(input_ids, parallel, offset)
         rows = torch.arange(batch, device=device)[:, None]
         native = self._native(x)
         step = self.pos_chunk or (NATIVE_QUERY_TILE if native else self._chunk_size(n))
@@ -292,7 +294,8 @@ class StackModel(nn.Module):
             for rd in self.reads:
                 # Collectives are never inside a checkpoint: every rank must
                 # issue the same sequence even when it supervises nothing.
-                z = self._dense_round(rd, z, k, v, positions, parallel)
+                with trace.phase("read_round"):
+                    z = self._dense_round(rd, z, k, v, positions, parallel)
             for j in range(0, hi - lo, loss_step):
                 labels = picked[:, lo + j:min(lo + j + loss_step, hi)]
                 hidden = z[:, j:j + loss_step]

@@ -36,6 +36,7 @@ from ..models.baseline import BaselineModel
 from ..models.stack import StackModel
 from ..parallel.context import ParallelContext, init_distributed, sum_all
 from . import checkpoint as ckpt
+from . import trace
 from .faults import maybe_fail
 from .inference import InferenceSession
 from .memory import GiB, training_estimate
@@ -146,7 +147,7 @@ class Trainer:
         offload = torch.autograd.graph.save_on_cpu(pin_memory=True) if args.activation_offload \
             else contextlib.nullcontext()
         with sync:
-            with amp, offload:
+            with amp, offload, trace.phase("forward"):
                 result = self.wrapped(ids, sup=mask, targets=target, parallel=parallel, offset=offset)
                 count = sum_all(result["count"])
                 if int(count) == 0:
@@ -155,14 +156,16 @@ class Trainer:
             maybe_fail("before_backward")
             if not bool(torch.isfinite(sum_all(scaled.detach()))):
                 raise FloatingPointError("non-finite loss across ranks; optimizer step was not applied")
-            scaled.backward()
+            with trace.phase("backward"):
+                scaled.backward()
         return torch.stack((result["loss_sum"].detach().double(), result["count"].double(),
                             result["correct"].double()))
 
     def finish_step(self):
         norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.args.clip_grad,
                                               error_if_nonfinite=True)
-        self.optimizer.step()
+        with trace.phase("optimizer"):
+            self.optimizer.step()
         # Parameters changed (locally, or by a ZeRO broadcast that bypasses the
         # version counters): drop the per-step low-precision weight copies.
         fused.clear_cast_cache()
@@ -215,6 +218,10 @@ def train(args, model, parallel, ck, dataset, validation_dataset=None):
         torch.cuda.reset_peak_memory_stats(device)
     stats = torch.zeros(3, device=device, dtype=torch.float64)
     window_start, window_steps = time.perf_counter(), 0
+    profiler = None
+    if getattr(args, "profile", ""):
+        from .trace import StepProfiler
+        profiler = StepProfiler(args.profile, parallel.rank)
     for step in range(start, args.steps):
         if graphed:
             ids, target, mask, _ = make_batch(args, generator, dataset)
@@ -228,6 +235,8 @@ def train(args, model, parallel, ck, dataset, validation_dataset=None):
                 stats += trainer.micro_step(ids, target, mask, last=micro == args.grad_accum - 1).to(device)
             norm = trainer.finish_step()
         window_steps += 1
+        if profiler is not None:
+            profiler.step()
         if (step + 1) % args.log_every == 0 or step == args.steps - 1:
             totals = sum_all(stats)
             if device.type == "cuda":
@@ -262,6 +271,8 @@ def train(args, model, parallel, ck, dataset, validation_dataset=None):
             emit({"event": "early_stop", "step": step + 1, "exact": round(record["exact"], 4)},
                  args, parallel.rank)
             break
+    if profiler is not None:
+        emit({"event": "profile", **profiler.summary()}, args, parallel.rank)
     if graphed:
         trainer.close()
 

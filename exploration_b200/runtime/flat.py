@@ -27,6 +27,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import _native, fused
+from . import trace
 
 ALIGN = 64            # elements: 256-byte aligned parameter views
 
@@ -357,7 +358,7 @@ class GraphTrainer:
         self.flat.zero_grad()
         amp = torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.args.precision == "bf16",
                              cache_enabled=False)
-        with amp:
+        with amp, trace.phase("forward"):
             result = self.model.forward_loss(ids, tgt, sup=mask, parallel=parallel, offset=self.offset,
                                              static_width=True)
         totals = torch.stack((result["loss_sum"].detach().float(), result["count"].float()))
@@ -366,11 +367,14 @@ class GraphTrainer:
         loss = result["loss_sum"] / totals[1].clamp_min(1.0)
         if self.buckets is not None:
             self.buckets.start()
-        loss.backward()
-        if self.buckets is not None:
-            self.buckets.finish()
+        with trace.phase("backward"):
+            loss.backward()
+        with trace.phase("gradient_reduction"):
+            if self.buckets is not None:
+                self.buckets.finish()
         check = totals[0] / totals[1]               # non-finite (or 0/0 with no tokens) skips the update
-        opt.reduce_and_step(check, reduced=self.buckets is not None)
+        with trace.phase("optimizer"):
+            opt.reduce_and_step(check, reduced=self.buckets is not None)
         stats = torch.cat((torch.stack((result["loss_sum"].detach().double(), result["count"].double(),
                                         result["correct"].double(), opt.hyper[3].double())),
                            totals.double()))

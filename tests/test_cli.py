@@ -142,3 +142,16 @@ def test_reference_configs_parse():
     for name in ("stack_2m", "stack_100m", "stack_500m", "baseline_2m"):
         args = parse_args(["plan", "--config", str(root / f"{name}.json")])
         assert args.dim > 0
+
+
+def test_train_profile_writes_a_trace(tmp_path):
+    out = io.StringIO()
+    common = ["--task", "random", "--vocab-size", "31", "--dim", "16", "--heads", "2", "--block-size", "4",
+              "--arch", "L,G", "--length", "17", "--batch-size", "2"]
+    with contextlib.redirect_stdout(out):
+        main(["train", *common, *CPU, "--steps", "6", "--log-every", "100", "--save", "",
+              "--profile", str(tmp_path / "prof")])
+    events = [json.loads(line) for line in out.getvalue().splitlines() if line.startswith("{")]
+    profile = [e for e in events if e.get("event") == "profile"]
+    assert profile and Path(profile[0]["trace"]).exists()
+    assert profile[0]["top"]
