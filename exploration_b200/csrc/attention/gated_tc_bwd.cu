@@ -39,7 +39,6 @@ namespace {
 using namespace sm100;
 
 constexpr int kT = 128;            // rows (queries or keys) per CTA and per tile
-constexpr int kThreads = 256;
 constexpr int kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -139,13 +138,13 @@ EB_DEVICE void load_row32(uint32_t addr, float (&x)[32]) {
 // folded into one FFMA per exponent and no local terms exist.
 template <int B, typename Sink>
 EB_DEVICE void grad_row(uint32_t s_addr, uint32_t dp_addr, int k0, int keys, const RowStats& st,
-                        float scale_log2, float scale, bool fast, Sink&& sink) {
+                        float scale_log2, float scale, bool fast, int c_begin, int c_end, Sink&& sink) {
   const bool live = st.pos >= 0;
   if constexpr (B <= 32) {
     constexpr int kSeg = 32 / B;
     if (fast) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < kT; c0 += 32) {
+      for (int c0 = c_begin; c0 < c_end; c0 += 32) {
         float a[32], dp[32], p[32], da[32];
         load_row32(s_addr + c0, a);
         load_row32(dp_addr + c0, dp);
@@ -182,7 +181,7 @@ EB_DEVICE void grad_row(uint32_t s_addr, uint32_t dp_addr, int k0, int keys, con
       return;
     }
 #pragma unroll 1
-    for (int c0 = 0; c0 < kT; c0 += 32) {
+    for (int c0 = c_begin; c0 < c_end; c0 += 32) {
       float a[32], dp[32], p[32], da[32];
       load_row32(s_addr + c0, a);
       load_row32(dp_addr + c0, dp);
@@ -238,8 +237,8 @@ EB_DEVICE void grad_row(uint32_t s_addr, uint32_t dp_addr, int k0, int keys, con
       rb[g] = 0.f;
     }
     // Pass A: online block max / mass.
-#pragma unroll
-    for (int c = 0; c < kT / 32; ++c) {
+#pragma unroll 1
+    for (int c = c_begin / 32; c < c_end / 32; ++c) {
       float a[32];
       load_row32(s_addr + c * 32, a);
       const int g = c / kChunks;
@@ -276,7 +275,7 @@ EB_DEVICE void grad_row(uint32_t s_addr, uint32_t dp_addr, int k0, int keys, con
     };
     // Pass B: block sums of the direct term.
 #pragma unroll 1
-    for (int c = 0; c < kT / 32; ++c) {
+    for (int c = c_begin / 32; c < c_end / 32; ++c) {
       float a[32], dp[32], p[32], e[32];
       bool remote;
       load_row32(s_addr + c * 32, a);
@@ -289,7 +288,7 @@ EB_DEVICE void grad_row(uint32_t s_addr, uint32_t dp_addr, int k0, int keys, con
     }
     // Pass C: dA.
 #pragma unroll 1
-    for (int c = 0; c < kT / 32; ++c) {
+    for (int c = c_begin / 32; c < c_end / 32; ++c) {
       float a[32], dp[32], p[32], e[32], da[32];
       bool remote;
       load_row32(s_addr + c * 32, a);
@@ -344,14 +343,22 @@ struct alignas(1024) DqSmem {
   int abort;
 };
 
-template <int D, int B>
-__global__ void __launch_bounds__(kThreads, 1)
+// SPLIT = number of gradient warpgroups: with 2 (blocks of at most 64 keys)
+// each warpgroup owns 64 of the 128 key columns of every tile, so a row's
+// work is done by two threads at once; no value crosses the column halves.
+constexpr int threads_for(int split) { return 128 + 128 * split; }
+
+template <int D, int B, int SPLIT>
+__global__ void __launch_bounds__(threads_for(SPLIT), 1)
 gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tg,
                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, BwdParams p) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
   DqSmem<D>& sm = *reinterpret_cast<DqSmem<D>*>(
       (reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr int kHalves = D / 64, kBox = 128 * 64;
+  // dA (bf16) lives in its own TMEM columns when two warpgroups write it
+  // concurrently (one warpgroup's dA may not overwrite the other's S).
+  constexpr uint32_t kDaCol = SPLIT == 2 ? 384 : 0;
   const int q_tile = gridDim.x - 1 - blockIdx.x;
   const int head = blockIdx.y, batch = blockIdx.z;
   const int q0 = q_tile * kT;
@@ -364,7 +371,7 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       mbar_init(&sm.kv_empty[s], 1);
     }
     mbar_init(&sm.sdp_full, 1);
-    mbar_init(&sm.da_full, 128);
+    mbar_init(&sm.da_full, 128 * SPLIT);
     mbar_init(&sm.dq_done, 1);
     sm.abort = 0;
     fence_barrier_init();
@@ -426,15 +433,17 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk)
-          mma_ts(tmem + 256, tmem + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kBox * 2, 1024), id_dq,
+          mma_ts(tmem + 256, tmem + kDaCol + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kBox * 2, 1024), id_dq,
                  (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&sm.kv_empty[s]);
         tc_commit(&sm.dq_done);
       }
     }
   } else if (warp >= 4) {
-    const int row = threadIdx.x - 128;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
+    const int wg = (warp - 4) >> 2;
+    const int row = (threadIdx.x - 128) & (kT - 1);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(((warp - 4) & 3) * 32) << 16);
+    const int c_begin = SPLIT == 2 ? wg * 64 : 0, c_end = SPLIT == 2 ? c_begin + 64 : kT;
     RowStats st = row_stats(p, batch, head, q0 + row);
     finish_stats<B>(st);
     bool ok = true;
@@ -445,12 +454,12 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       }
       tc_fence_after();
       const bool fast = (j + 1) * kT <= bnd[2] && (j + 1) * kT <= p.keys;
-      grad_row<B>(lane_addr, lane_addr + 128, j * kT, p.keys, st, p.scale_log2, p.scale, fast,
+      grad_row<B>(lane_addr, lane_addr + 128, j * kT, p.keys, st, p.scale_log2, p.scale, fast, c_begin, c_end,
                   [&](int c0, const float (&pv)[32], const float (&da)[32]) {
                     uint32_t packed[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) packed[i] = pack_bf16(da[2 * i], da[2 * i + 1]);
-                    tmem_st16(lane_addr + c0 / 2, packed);
+                    tmem_st16(lane_addr + kDaCol + c0 / 2, packed);
                   });
       tc_wait_st();
       tc_fence_before();
@@ -463,8 +472,10 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     const int q = q0 + row;
     const bool write = q < p.queries;
     __nv_bfloat16* out = p.dq + ((static_cast<int64_t>(batch) * p.queries + (write ? q : 0)) * p.heads + head) * D;
+    constexpr int kCols = SPLIT == 2 ? D / 2 : D;   // dQ columns stored by this warpgroup
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int cc = 0; cc < kCols; cc += 32) {
+      const int c = (SPLIT == 2 ? wg * kCols : 0) + cc;
       float x[32];
       if (have) {
         load_row32(lane_addr + 256 + c, x);
@@ -509,8 +520,8 @@ struct alignas(1024) DkvSmem {
 // Byte offset of (row, 16-byte chunk) in a [128 rows x 64 bf16] 128B-swizzled box.
 EB_DEVICE uint32_t sw128_offset(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
-template <int D, int B>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int B, int SPLIT>
+__global__ void __launch_bounds__(threads_for(SPLIT), 1)
 gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tg,
                     const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, BwdParams p) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
@@ -526,7 +537,7 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     mbar_init(&sm.qg_full, 1);
     mbar_init(&sm.qg_free, 1);
     mbar_init(&sm.sdp_full, 1);
-    mbar_init(&sm.pda_full, 128);
+    mbar_init(&sm.pda_full, 128 * SPLIT);
     mbar_init(&sm.acc_done, 1);
     sm.abort = 0;
     fence_barrier_init();
@@ -601,8 +612,10 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       }
     }
   } else if (warp >= 4) {
-    const int row = threadIdx.x - 128;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
+    const int wg = (warp - 4) >> 2;
+    const int row = (threadIdx.x - 128) & (kT - 1);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(((warp - 4) & 3) * 32) << 16);
+    const int c_begin = SPLIT == 2 ? wg * 64 : 0, c_end = SPLIT == 2 ? c_begin + 64 : kT;
     uint8_t* pt = reinterpret_cast<uint8_t*>(sm.pt);
     uint8_t* dat = reinterpret_cast<uint8_t*>(sm.dat);
     bool ok = true;
@@ -618,7 +631,7 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       tc_fence_after();
       const int local_start_i = p.bounds[(static_cast<int64_t>(batch) * p.q_tiles + i) * 3 + 2];
       const bool fast = k0 + kT <= local_start_i && k0 + kT <= p.keys;
-      grad_row<B>(lane_addr, lane_addr + 128, k0, p.keys, st, p.scale_log2, p.scale, fast,
+      grad_row<B>(lane_addr, lane_addr + 128, k0, p.keys, st, p.scale_log2, p.scale, fast, c_begin, c_end,
                   [&](int c0, const float (&pv)[32], const float (&da)[32]) {
                     const int box = c0 / 64, chunk0 = (c0 % 64) / 8;
 #pragma unroll
@@ -647,6 +660,7 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     const int64_t base = ((static_cast<int64_t>(batch) * p.keys + (write ? key : 0)) * p.heads + head) * D;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
+      if (SPLIT == 2 && which != wg) continue;       // warpgroup 0 stores dK, warpgroup 1 dV
       __nv_bfloat16* out = (which == 0 ? p.dk : p.dv) + base;
 #pragma unroll
       for (int c = 0; c < D; c += 32) {
@@ -683,17 +697,21 @@ void launch_bwd(const at::Tensor& grad, const at::Tensor& q, const at::Tensor& k
   CUtensorMap tg = make_bhld_map(grad.data_ptr(), batch, queries, heads, D, kT);
   CUtensorMap tk = make_bhld_map(k.data_ptr(), batch, keys, heads, D, kT);
   CUtensorMap tv = make_bhld_map(v.data_ptr(), batch, keys, heads, D, kT);
+  // Two gradient warpgroups when a gate block fits in a column half.
+  constexpr int kSplit = B <= 64 ? 2 : 1;
   {
     const size_t smem = sizeof(DqSmem<D>) + 1024;
-    auto kernel = gated_dq_tc_kernel<D, B>;
+    auto kernel = gated_dq_tc_kernel<D, B, kSplit>;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kernel<<<dim3((queries + kT - 1) / kT, heads, batch), kThreads, smem, stream>>>(tq, tg, tk, tv, params);
+    kernel<<<dim3((queries + kT - 1) / kT, heads, batch), threads_for(kSplit), smem, stream>>>(tq, tg, tk, tv,
+                                                                                               params);
   }
   {
     const size_t smem = sizeof(DkvSmem<D>) + 1024;
-    auto kernel = gated_dkv_tc_kernel<D, B>;
+    auto kernel = gated_dkv_tc_kernel<D, B, kSplit>;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kernel<<<dim3((keys + kT - 1) / kT, heads, batch), kThreads, smem, stream>>>(tq, tg, tk, tv, params);
+    kernel<<<dim3((keys + kT - 1) / kT, heads, batch), threads_for(kSplit), smem, stream>>>(tq, tg, tk, tv,
+                                                                                            params);
   }
 }
 
@@ -816,11 +834,11 @@ void noalloc_launch(const void* grad, const void* q, const void* k, const void* 
   CUtensorMap tk = make_bhld_map(const_cast<void*>(k), batch, keys, heads, D, kT);
   CUtensorMap tv = make_bhld_map(const_cast<void*>(v), batch, keys, heads, D, kT);
   const size_t smem_q = sizeof(DqSmem<D>) + 1024, smem_kv = sizeof(DkvSmem<D>) + 1024;
-  cudaFuncSetAttribute(gated_dq_tc_kernel<D, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-  cudaFuncSetAttribute(gated_dkv_tc_kernel<D, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-  gated_dq_tc_kernel<D, B><<<dim3((queries + kT - 1) / kT, heads, batch), kThreads, smem_q, stream>>>(
+  cudaFuncSetAttribute(gated_dq_tc_kernel<D, B, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+  cudaFuncSetAttribute(gated_dkv_tc_kernel<D, B, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+  gated_dq_tc_kernel<D, B, 1><<<dim3((queries + kT - 1) / kT, heads, batch), threads_for(1), smem_q, stream>>>(
       tq, tg, tk, tv, params);
-  gated_dkv_tc_kernel<D, B><<<dim3((keys + kT - 1) / kT, heads, batch), kThreads, smem_kv, stream>>>(
+  gated_dkv_tc_kernel<D, B, 1><<<dim3((keys + kT - 1) / kT, heads, batch), threads_for(1), smem_kv, stream>>>(
       tq, tg, tk, tv, params);
 }
 

@@ -825,6 +825,7 @@ std::vector<at::Tensor> local_tc_fwd(const at::Tensor& qkv, const c10::optional<
   const size_t smem = std::max<size_t>(sizeof(LtSmem) + 1024, 80 * 1024);
   auto kernel = local_tc_fwd_kernel;
   EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   dim3 grid((n + kM - 1) / kM, heads, batch);
   kernel<<<grid, kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(t_main, t_halo, t_prev, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -882,6 +883,8 @@ std::vector<at::Tensor> local_tc_bwd(const at::Tensor& dout, const at::Tensor& q
     const size_t smem = std::max<size_t>(sizeof(LtDqSmem) + 1024, 80 * 1024);
     auto kernel = local_tc_dq_kernel;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    // Two CTAs per SM need the maximum shared-memory carveout.
+    EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     trace("dq attribute");
     kernel<<<dim3(ctas, heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout, args);
     C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -260,9 +260,9 @@ def test_gated_forward_two_tile_kernel_matches_single(n, b, monkeypatch):
     pos[1, n // 3:] = pos[1, n // 3:].flip(0)          # not monotone in the second row
     pos[1, 5] = -1
     with torch.no_grad():
-        two = dense_attention(q, k, v, pos, b, "cuda")
-        monkeypatch.setenv("EB200_GATED_FWD", "single")
         one = dense_attention(q, k, v, pos, b, "cuda")
+        monkeypatch.setenv("EB200_GATED_FWD", "two")
+        two = dense_attention(q, k, v, pos, b, "cuda")
     torch.testing.assert_close(two.float(), one.float(), atol=2e-2, rtol=2e-2)
 
 
