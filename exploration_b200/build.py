@@ -38,6 +38,7 @@ SOURCES = [
     "sparse/block_scores_tc.cu",
     "gemm/gemm_tc.cu",
     "comm/symm_heap.cu",
+    "comm/grad_reduce.cu",
 ]
 
 CUDA_FLAGS = [

@@ -69,6 +69,17 @@ void flat_adamw(at::Tensor& param, const at::Tensor& grad, at::Tensor& exp_avg, 
                 const c10::optional<at::Tensor>& loss_check, double beta1, double beta2, double eps,
                 double decay);
 void flat_cast_bf16(const at::Tensor& x, at::Tensor& out);
+int64_t grad_flag_bytes();
+int64_t grad_reduce_max_buckets();
+void grad_reduce_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags, int64_t rank,
+                        int64_t bucket, int64_t lo, int64_t hi, int64_t q, bool all_reduce, double scale,
+                        at::Tensor& partial, double timeout_s);
+void grad_norm_exchange(const at::Tensor& partial, const std::vector<int64_t>& flags, int64_t rank, at::Tensor& hyper,
+                        double timeout_s);
+void flat_adamw_peer(at::Tensor& param, const at::Tensor& grad, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
+                     const std::vector<int64_t>& shadows, int64_t rank, const at::Tensor& hyper,
+                     const c10::optional<at::Tensor>& loss_check, double beta1, double beta2, double eps,
+                     double decay);
 bool local_tc_supported(const at::Tensor& qkv, int64_t block);
 std::vector<at::Tensor> local_tc_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& prev, int64_t start,
                                      int64_t valid_start, int64_t n);
@@ -129,6 +140,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flat_sq_norm", &eb::flat_sq_norm, "hyper[3] = sum of squares of a flat fp32 buffer");
   m.def("flat_adamw", &eb::flat_adamw, "AdamW over a flat buffer with device-side lr/step/clip");
   m.def("flat_cast_bf16", &eb::flat_cast_bf16);
+  m.def("grad_flag_bytes", &eb::grad_flag_bytes);
+  m.def("grad_reduce_max_buckets", &eb::grad_reduce_max_buckets);
+  m.def("grad_reduce_bucket", &eb::grad_reduce_bucket,
+        "reduce one gradient bucket over NVLink peer memory (owned slice; fused norm partials)");
+  m.def("grad_norm_exchange", &eb::grad_norm_exchange, "global squared gradient norm; end-of-reduction barrier");
+  m.def("flat_adamw_peer", &eb::flat_adamw_peer, "AdamW over an owned slice with the bf16 shadow stored to every rank");
   m.def("local_tc_supported", &eb::local_tc_supported);
   m.def("local_tc_fwd", &eb::local_tc_fwd, "tcgen05 local halo attention forward (block 16, head dim 64, bf16)");
   m.def("local_tc_bwd", &eb::local_tc_bwd, "tcgen05 local halo attention backward (dQ kernel + dK/dV kernel)");

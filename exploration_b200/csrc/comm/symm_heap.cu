@@ -29,6 +29,7 @@
 #include <cstring>
 #include <vector>
 
+#include "../common/peer.cuh"
 #include "../common/sm100.cuh"
 #include "../common/tma.cuh"
 
@@ -47,22 +48,6 @@ struct SignalPtrs {
 struct SourcePtrs {
   const uint4* p[kMaxRanks];                    // rank r's slot
 };
-
-EB_DEVICE void store_release_sys(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-EB_DEVICE unsigned int load_acquire_sys(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-EB_DEVICE uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 
 __global__ void heap_barrier_kernel(SignalPtrs sig, int rank, int world, uint64_t timeout_ns, ErrorSlot* err) {
   __shared__ unsigned int epoch;

@@ -19,6 +19,8 @@ the GEMMs read a bf16 copy refreshed once per optimizer step.
 """
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import _native
@@ -55,6 +57,36 @@ def weight_grad(g, x):
     return torch.mm(g.t(), x, out_dtype=torch.float32)
 
 
+# id(param) -> (weak reference to param, callback). A registered parameter
+# receives its weight gradient straight into ``param.grad`` (the GEMM adds
+# into it, beta = 1) instead of through autograd's accumulation (a separate
+# read-add-write pass over the gradient); the callback then reports the
+# gradient complete, in place of a post-accumulate-grad hook.
+_grad_sinks: dict = {}
+
+
+def register_grad_sink(param, callback) -> None:
+    key = id(param)
+    _grad_sinks[key] = (weakref.ref(param, lambda _ref, k=key: _grad_sinks.pop(k, None)), callback)
+
+
+def remove_grad_sink(param) -> None:
+    _grad_sinks.pop(id(param), None)
+
+
+def accumulate_weight_grad(param, g, x):
+    """``dW = g^T x`` for ``param``: added into ``param.grad`` when it is a sink (returns
+    ``None``), else returned for autograd to accumulate."""
+    sink = _grad_sinks.get(id(param)) if param is not None else None
+    if (sink is not None and sink[0]() is param and g.is_cuda and param.grad is not None
+            and param.grad.dtype == torch.float32 and param.grad.is_contiguous()):
+        grad = param.grad.view(param.shape)
+        torch.addmm(grad, g.t(), x, out_dtype=torch.float32, out=grad)
+        sink[1](param)
+        return None
+    return weight_grad(g, x)
+
+
 def _bf16_weight(param):
     from .fused import _cached_copy
     return _cached_copy(param, torch.bfloat16)
@@ -76,6 +108,7 @@ class Linear(torch.autograd.Function):
         out = torch.mm(x2, w.t(), out_dtype=torch.float32) if out_f32 else torch.mm(x2, w.t())
         ctx.save_for_backward(x2, w)
         ctx.shape = x.shape
+        ctx.param = weight
         return out.view(*x.shape[:-1], w.shape[0])
 
     @staticmethod
@@ -84,7 +117,7 @@ class Linear(torch.autograd.Function):
         x2, w = ctx.saved_tensors
         g = _flat(dy).to(torch.bfloat16)
         dx = g @ w
-        return dx.view(ctx.shape), weight_grad(g, x2), None
+        return dx.view(ctx.shape), accumulate_weight_grad(ctx.param, g, x2), None
 
 
 class LinearResidual(torch.autograd.Function):
@@ -98,6 +131,7 @@ class LinearResidual(torch.autograd.Function):
         out = torch.empty(res.shape, device=x.device, dtype=torch.float32)
         gemm(x2, False, w, False, out, BIAS_RESIDUAL, bias=bias, residual=res)
         ctx.save_for_backward(x2, w)
+        ctx.param = weight
         ctx.has_bias = bias is not None
         ctx.shape = x.shape
         return out.view(residual.shape)
@@ -109,7 +143,7 @@ class LinearResidual(torch.autograd.Function):
         d32 = _flat(dout)
         g = d32.to(torch.bfloat16)
         dx = g @ w
-        dw = weight_grad(g, x2)
+        dw = accumulate_weight_grad(ctx.param, g, x2)
         db = d32.sum(0) if ctx.has_bias else None
         return dx.view(ctx.shape), dw, db, dout
 
@@ -129,6 +163,7 @@ class FFNResidual(torch.autograd.Function):
         out = torch.empty(y2.shape, device=h.device, dtype=torch.float32)
         gemm(u, False, w2b, False, out, BIAS_RESIDUAL, bias=b2, residual=y2)
         ctx.save_for_backward(h2, dgelu, u, w1b, w2b)
+        ctx.params = (w1, w2)
         ctx.shape = h.shape
         return out.view(y.shape)
 
@@ -139,12 +174,12 @@ class FFNResidual(torch.autograd.Function):
         d32 = _flat(dout)
         g = d32.to(torch.bfloat16)
         db2 = d32.sum(0)
-        dw2 = weight_grad(g, u)
+        dw2 = accumulate_weight_grad(ctx.params[1], g, u)
         dh_pre = torch.empty_like(dgelu)
         partial = torch.empty(-(-g.shape[0] // TILE_M), dgelu.shape[1], device=g.device, dtype=torch.float32)
         gemm(g, False, w2b, True, dh_pre, GELU_BACK, aux=dgelu, partial=partial)
         db1 = partial.sum(0)
-        dw1 = weight_grad(dh_pre, h2)
+        dw1 = accumulate_weight_grad(ctx.params[0], dh_pre, h2)
         dh = dh_pre @ w1b
         return dh.view(ctx.shape), dout, dw1, db1, dw2, db2
 

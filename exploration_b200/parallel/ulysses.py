@@ -53,6 +53,7 @@ class _ProjectToHeads(torch.autograd.Function):
         heap.barrier()
         out = heap.tensor(slot, (parts, batch, n_local * U.world, heads_per_rank, head_dim))
         ctx.save_for_backward(x2, w)
+        ctx.param = weight
         ctx.meta = (U, parts, batch, n_local, C, x.shape)
         return out
 
@@ -71,7 +72,7 @@ class _ProjectToHeads(torch.autograd.Function):
         U.ext.gemm_gather(ptrs, U.rank, parts, batch, n_local, C, w, True, dx, G.STORE_BF16, None, None)
         dy_seq = torch.empty(batch * n_local, parts * U.world * C, device=x2.device, dtype=torch.bfloat16)
         U.ext.gather_rows(ptrs, U.rank, parts, batch, n_local, C, dy_seq)
-        dw = G.weight_grad(dy_seq, x2)
+        dw = G.accumulate_weight_grad(ctx.param, dy_seq, x2)
         return dx.view(shape), dw, None, None, None, None
 
 
@@ -92,6 +93,7 @@ class _HeadsToLinearResidual(torch.autograd.Function):
         U.ext.gemm_gather(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, w, False, out,
                           G.BIAS_RESIDUAL, bias, res)
         ctx.save_for_backward(w)
+        ctx.param = weight
         ctx.meta = (U, slot, batch, n_local, hpr, hd, bias is not None)
         return out.view(residual.shape)
 
@@ -111,7 +113,7 @@ class _HeadsToLinearResidual(torch.autograd.Function):
         dheads = heap.tensor(gslot, (batch, n_local * U.world, hpr, hd))
         ctx_seq = torch.empty(batch * n_local, U.world * C, device=g.device, dtype=torch.bfloat16)
         U.ext.gather_rows(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, ctx_seq)
-        dw = G.weight_grad(g, ctx_seq)
+        dw = G.accumulate_weight_grad(ctx.param, g, ctx_seq)
         db = d32.sum(0) if has_bias else None
         return dheads, dw, db, dout, None
 

@@ -100,7 +100,7 @@ def train_cp2(rank, world):
     return "finished"
 
 
-def _flat_vs_eager(parallel, shard):
+def _flat_vs_eager(parallel, shard, layout="contiguous"):
     """Three steps of the flat (graph-ready) trainer against the eager trainer."""
     import copy
     import torch
@@ -122,6 +122,15 @@ def _flat_vs_eager(parallel, shard):
     eager_model, flat_model = copy.deepcopy(base), copy.deepcopy(base)
     eager = Trainer(args, eager_model, parallel)
     flat = GraphTrainer(args, flat_model, parallel, use_graph=False)
+    if layout == "buckets":
+        # The peer-reduction layout: a slice of every (small) bucket per rank.
+        from exploration_b200.runtime.flat import FlatAdamW, _bucket_bounds, bucket_layout
+        bounds, _ = _bucket_bounds(flat.flat, 4096, split_boundary=True)
+        _, shard_layout = bucket_layout(flat.flat, bounds, world, parallel.rank, shard)
+        assert shard_layout is None or len(shard_layout.groups) > 2
+        opt = flat.optimizer
+        flat.optimizer = FlatAdamW(flat.flat, args.lr, opt.betas, weight_decay=args.weight_decay,
+                                   max_norm=args.clip_grad, shard=shard, layout=shard_layout)
     gen_a = torch.Generator().manual_seed(5 + parallel.dp_rank)
     gen_b = torch.Generator().manual_seed(5 + parallel.dp_rank)
     for step in range(3):
@@ -137,6 +146,16 @@ def _flat_vs_eager(parallel, shard):
         assert torch.allclose(a, b, rtol=1e-5, atol=1e-5), (step, a, b)
     for (name, p), q in zip(eager_model.named_parameters(), flat_model.parameters()):
         assert torch.allclose(p, q, rtol=1e-4, atol=1e-6), name
+    # Optimizer state round trip through the torch.optim.AdamW layout (collective).
+    state = flat.optimizer.state_dict()
+    assert all(entry["exp_avg_sq"].abs().sum() > 0 for entry in state["state"].values())
+    from exploration_b200.runtime.flat import FlatAdamW
+    fresh = FlatAdamW(flat.flat, args.lr, shard=shard)
+    fresh.load_state_dict(state)
+    reloaded = fresh.state_dict()
+    for i in state["state"]:
+        assert torch.equal(reloaded["state"][i]["exp_avg"], state["state"][i]["exp_avg"])
+        assert torch.equal(reloaded["state"][i]["exp_avg_sq"], state["state"][i]["exp_avg_sq"])
     flat.close()
     return world
 
@@ -146,8 +165,9 @@ def flat_trainer(rank, world):
     from exploration_b200.parallel.context import ParallelContext
     cp = int(os.environ["TEST_CP"])
     shard = os.environ.get("TEST_SHARD") == "1"
+    layout = os.environ.get("TEST_LAYOUT", "contiguous")
     parallel = ParallelContext.initialize(cp, "cpu")
     try:
-        return _flat_vs_eager(parallel, shard)
+        return _flat_vs_eager(parallel, shard, layout)
     finally:
         dist.destroy_process_group()

@@ -5,6 +5,8 @@ parallelism, once through the NVLink-fused Ulysses exchange and once through
 the NCCL all-to-all path, on identical weights and data; every rank compares
 its loss and local parameter gradients and reports the largest differences.
 ``train``: a few optimizer steps through the engine with the fused exchange.
+``graph``: graph-captured steps against eager steps. ``peer_grad``: the
+peer-memory gradient reduction against the NCCL path.
 """
 import json
 import os
@@ -123,13 +125,67 @@ def graph(world, rank, device):
     return {"loss_diffs": diffs, "captured": captured, "device_errors": list(errors)}
 
 
+def peer_grad(world, rank, device):
+    """Graph-captured steps with the peer-memory gradient reduction against the NCCL path.
+
+    Two trainers on copies of one model and identical batches: ``EB200_P2P_GRAD=1``
+    (per-bucket reduce-scatter kernels over NVLink, fused norm, shadows stored to
+    every rank by the update) and ``EB200_P2P_GRAD=0`` (NCCL bucketed all-reduce,
+    shadow all-gather). Both shard the optimizer (ZeRO-1) or both do not.
+    """
+    import copy
+    from exploration_b200.cli import parse_args
+    from exploration_b200.runtime.engine import lr_factor, make_batch
+    from exploration_b200.runtime.flat import GraphTrainer
+    shard = os.environ.get("TEST_SHARD", "1") == "1"
+    args = parse_args(["train", "--dim", "256", "--heads", "8", "--block-size", "16", "--arch", "Lx2,G",
+                       "--task", "random", "--length", str(512 * world), "--batch-size", "1",
+                       "--precision", "bf16", "--backend", "cuda", "--context-parallel", str(world),
+                       "--steps", "5", "--save", "", "--no-checkpoint-chunks", "--clip-grad", "0.5",
+                       "--optimizer-shard" if shard else "--no-optimizer-shard"])
+    parallel = ParallelContext.initialize(world, "cuda")
+    base = _model(device)
+    peer_model, nccl_model = copy.deepcopy(base), copy.deepcopy(base)
+    os.environ["EB200_P2P_GRAD"] = "1"
+    peer = GraphTrainer(args, peer_model, parallel)
+    os.environ["EB200_P2P_GRAD"] = "0"
+    nccl = GraphTrainer(args, nccl_model, parallel)
+    assert peer.peer and not nccl.peer
+    gen_a, gen_b = torch.Generator().manual_seed(100), torch.Generator().manual_seed(100)
+    loss_diffs, norm_diffs = [], []
+    for step in range(args.steps):
+        lr = args.lr * lr_factor(step, args.steps)
+        ids, target, mask, _ = make_batch(args, gen_a)
+        a, norm_a = peer.step(ids, target, mask, lr)
+        ids, target, mask, _ = make_batch(args, gen_b)
+        b, norm_b = nccl.step(ids, target, mask, lr)
+        loss_diffs.append(abs(float(a[0] / a[1]) - float(b[0] / b[1])))
+        norm_diffs.append(abs(norm_a - norm_b) / max(norm_b, 1e-6))
+    worst = 0.0
+    for p, q in zip(peer_model.parameters(), nccl_model.parameters()):
+        worst = max(worst, (p.detach() - q.detach()).abs().max().item())
+    # Every rank's bf16 shadows agree after the peer stores (they are what the GEMMs read).
+    shadow = peer.flat.shadow.float()
+    gathered = [torch.empty_like(shadow) for _ in range(world)]
+    dist.all_gather(gathered, shadow)
+    shadows_equal = all(torch.equal(gathered[0], t) for t in gathered[1:])
+    captured = peer.graph is not None
+    peer.close()
+    nccl.close()
+    errors = _native.load().device_errors(device.index)
+    parallel.close()
+    return {"loss_diffs": loss_diffs, "norm_diffs": norm_diffs, "worst_param_diff": worst,
+            "shadows_equal": shadows_equal, "captured": captured, "device_errors": list(errors)}
+
+
 def main():
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     device = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
     torch.cuda.set_device(device)
     torch.backends.cuda.matmul.allow_tf32 = False
-    result = {"parity": parity, "train": train, "graph": graph}[sys.argv[1]](world, rank, device)
+    result = {"parity": parity, "train": train, "graph": graph,
+              "peer_grad": peer_grad}[sys.argv[1]](world, rank, device)
     gathered = [None] * world
     dist.all_gather_object(gathered, result)
     if rank == 0:

@@ -73,9 +73,12 @@ def test_injected_rank_failure_ends_every_rank():
     assert out.get(0, ("error", "no report"))[0] == "error"
 
 
-@pytest.mark.parametrize("cp,shard", [(2, "0"), (1, "1"), (2, "1")])
-def test_flat_trainer_matches_eager(cp, shard):
-    out = launch("flat_trainer", 2, {"TEST_CP": str(cp), "TEST_SHARD": shard})
+@pytest.mark.parametrize("cp,shard,layout", [(2, "0", "contiguous"), (1, "1", "contiguous"), (2, "1", "contiguous"),
+                                             (2, "1", "buckets"), (1, "0", "buckets")])
+def test_flat_trainer_matches_eager(cp, shard, layout):
+    """``buckets``: the optimizer updates a slice of every gradient bucket per rank (the
+    layout of the peer-memory reduction), including the checkpoint state round trip."""
+    out = launch("flat_trainer", 2, {"TEST_CP": str(cp), "TEST_SHARD": shard, "TEST_LAYOUT": layout})
     assert len(out) == 2, out
     for rank, (status, payload) in out.items():
         assert status == "ok", payload

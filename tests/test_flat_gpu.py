@@ -76,3 +76,45 @@ def test_graph_trainer_matches_eager(native):
     finally:
         graph.close()
     assert native.device_errors(0) == (0, 0)
+
+
+def test_peer_reduction_kernels_single_rank(native):
+    """The peer-memory reduction kernels on one rank: scale, norm partials, epochs, shadow stores."""
+    from exploration_b200.parallel.symmetric import SymmetricHeap
+    n, ctas = 64 * 1000, 32
+    heap = SymmetricHeap(None, torch.device("cuda", 0), n * 6 + native.grad_flag_bytes() + (1 << 16))
+    try:
+        goff = heap.alloc(n * 4)
+        soff = heap.alloc(n * 2)
+        foff = heap.alloc(native.grad_flag_bytes())
+        grad = heap.tensor(goff, [n], torch.float32)
+        shadow = heap.tensor(soff, [n], torch.bfloat16)
+        g = torch.Generator(device="cuda").manual_seed(1)
+        partial = torch.zeros(2 * ctas, device="cuda")
+        hyper = torch.tensor([1e-3, 1.0, 0.0, 0.0], device="cuda")
+        for step in range(3):                      # epochs advance on every exchange
+            src = torch.randn(n, device="cuda", generator=g)
+            grad.copy_(src)
+            bounds = [(0, 64 * 400), (64 * 400, n)]
+            for b in (1, 0):
+                lo, hi = bounds[b]
+                native.grad_reduce_bucket([heap.base + goff], [heap.base + foff], 0, b, lo, hi, hi - lo, b == 0,
+                                          0.5, partial[b * ctas:(b + 1) * ctas], 5.0)
+            native.grad_norm_exchange(partial, [heap.base + foff], 0, hyper, 5.0)
+            torch.cuda.synchronize()
+            torch.testing.assert_close(grad, src * 0.5, rtol=0, atol=0)
+            torch.testing.assert_close(hyper[3], (src * 0.5).double().pow(2).sum().float(), rtol=1e-5, atol=0)
+        # AdamW with the shadow stored through the peer table equals the local kernel.
+        p = torch.randn(n, device="cuda", generator=g)
+        m = torch.zeros(n, device="cuda")
+        v = torch.zeros(n, device="cuda")
+        p2, m2, v2 = p.clone(), m.clone(), v.clone()
+        local_shadow = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+        native.flat_adamw_peer(p, grad, m, v, [heap.base + soff], 0, hyper, None, 0.9, 0.95, 1e-8, 0.1)
+        native.flat_adamw(p2, grad, m2, v2, local_shadow, hyper, None, 0.9, 0.95, 1e-8, 0.1)
+        torch.cuda.synchronize()
+        assert torch.equal(p, p2) and torch.equal(m, m2) and torch.equal(v, v2)
+        assert torch.equal(shadow, local_shadow)
+        assert native.device_errors(0) == (0, 0)
+    finally:
+        heap.close()

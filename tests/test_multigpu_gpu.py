@@ -26,8 +26,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _launch(mode, world):
-    env = dict(os.environ, EB200_PG_TIMEOUT_S="60", EB200_PEER_TIMEOUT_S="5", NCCL_NVLS_ENABLE="0")
+def _launch(mode, world, extra=None):
+    env = dict(os.environ, EB200_PG_TIMEOUT_S="60", EB200_PEER_TIMEOUT_S="5", NCCL_NVLS_ENABLE="0",
+               **(extra or {}))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            str(WORKER), mode]
@@ -70,3 +71,14 @@ def test_graph_trainer_matches_eager_across_gpus():
         assert r["device_errors"] == [0, 0]
         assert r["captured"]
         assert max(r["loss_diffs"]) < 5e-2, r["loss_diffs"]
+
+
+@pytest.mark.parametrize("shard", ["1", "0"])
+def test_peer_gradient_reduction_matches_nccl(shard):
+    results = _launch("peer_grad", 2, {"TEST_SHARD": shard})
+    for r in results:
+        assert r["device_errors"] == [0, 0]
+        assert r["captured"] and r["shadows_equal"]
+        assert max(r["loss_diffs"]) < 2e-2, r["loss_diffs"]
+        assert max(r["norm_diffs"]) < 2e-2, r["norm_diffs"]
+        assert r["worst_param_diff"] < 5e-3, r["worst_param_diff"]
