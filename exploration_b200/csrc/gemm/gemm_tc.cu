@@ -90,12 +90,29 @@ struct alignas(1024) GemmSmem {
   float colsum[8][BN / 2]; // per epilogue warp column partials of the GELU-backward epilogue
 };
 
-// Exact GELU and its derivative from one erf: gelu(v) = v * Phi(v),
-// gelu'(v) = Phi(v) + v * phi(v) (Phi/phi: standard normal cdf/pdf).
+EB_DEVICE float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exact GELU and its derivative: gelu(v) = v * Phi(v), gelu'(v) = Phi(v) +
+// v * phi(v) (Phi/phi: standard normal cdf/pdf). erf comes from Abramowitz &
+// Stegun, Handbook of Mathematical Functions, formula 7.1.26 (absolute error
+// <= 1.5e-7, far below the bf16 rounding of both outputs):
+//   erf(x) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-x^2),
+//   t = 1 / (1 + p x), x >= 0.
+// With x = |v| / sqrt(2), exp(-x^2) = exp(-v^2 / 2) is also the exponential
+// of phi(v), so both outputs cost one exp2 and one reciprocal.
 EB_DEVICE void gelu_and_grad(float v, float& y, float& dy) {
-  const float cdf = 0.5f * (1.f + erff(v * 0.70710678118654752f));
+  const float x = fabsf(v) * 0.70710678118654752f;
+  const float t = rcp_approx(fmaf(0.3275911f, x, 1.f));
+  const float poly =
+      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+  const float e = ex2(v * v * -0.72134752044448170f);          // exp(-v^2 / 2) = 2^(-v^2 log2(e) / 2)
+  const float cdf = 0.5f + copysignf(0.5f - 0.5f * poly * e, v);
   y = v * cdf;
-  dy = cdf + v * expf(-0.5f * v * v) * 0.39894228040143268f;
+  dy = fmaf(v * e, 0.39894228040143268f, cdf);
 }
 
 EB_DEVICE float4 load_bias4(const float* bias, int n, int N) {
@@ -109,7 +126,7 @@ EB_DEVICE float4 load_bias4(const float* bias, int n, int N) {
 // Four consecutive outputs (m, n..n+3) of one row. Vector accesses need the
 // row start aligned (checked on the host: GemmArgs::vec) and n + 4 <= N.
 template <int EPI>
-EB_DEVICE void epilogue4(const GemmArgs& g, int m, int n, float4 v4, float4 b4, float (&cs)[4]) {
+EB_DEVICE void epilogue4(const GemmArgs& g, int m, int n, float4 v4, float4 b4, float (&cs)[4], uint2 aux_raw) {
   float v[4] = {v4.x, v4.y, v4.z, v4.w};
   const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
   const bool vec = g.vec && n + 4 <= g.N;
@@ -178,7 +195,7 @@ EB_DEVICE void epilogue4(const GemmArgs& g, int m, int n, float4 v4, float4 b4, 
     const __nv_bfloat16* a = g.aux + static_cast<int64_t>(m) * g.ld_aux + n;
     float pre[4] = {0.f, 0.f, 0.f, 0.f};
     if (vec) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(a);
+      const uint2 raw = aux_raw;               // loaded by the caller ahead of the TMEM wait
       const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
       const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
       pre[0] = __low2float(p0); pre[1] = __high2float(p0); pre[2] = __low2float(p1); pre[3] = __high2float(p1);
@@ -340,6 +357,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       for (int c0 = grp * (BN / 2); c0 < (grp + 1) * (BN / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + acc * BN + c0, r);
+        // GELU backward: the kept gelu' of this chunk's 8 (row, 4-column) groups is
+        // loaded while the TMEM load is in flight.
+        uint2 aux_raw[2][4];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            aux_raw[half][it] = make_uint2(0u, 0u);
+            if constexpr (EPI == kGeluBackBf16) {
+              const int m = tm * kBM + wr * 32 + it * 8 + rq;
+              const int n = tn * BN + c0 + half * 16 + 4 * u;
+              if (g.vec && m < g.M && n + 4 <= g.N)
+                aux_raw[half][it] = *reinterpret_cast<const uint2*>(g.aux + static_cast<int64_t>(m) * g.ld_aux + n);
+            }
+          }
+        }
         tc_wait_ld();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -362,7 +395,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             const int rr = it * 8 + rq;
             const float4 v = stage[rr * 4 + (u ^ ((rr >> 1) & 3))];
             const int m = tm * kBM + wr * 32 + rr;
-            if (m < g.M && n < g.N) epilogue4<EPI>(g, m, n, v, bias4, cs);
+            if (m < g.M && n < g.N) epilogue4<EPI>(g, m, n, v, bias4, cs, aux_raw[half][it]);
           }
           __syncwarp();
           if constexpr (EPI == kGeluBackBf16) {

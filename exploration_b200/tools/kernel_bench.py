@@ -2,7 +2,9 @@
 
 ``python -m exploration_b200.tools.kernel_bench`` prints CUDA-event timings
 (median of ``--iterations`` after ``--warmup``) of the local window
-attention, the gated dense attention and the fused GEMM layers for one
+attention, the gated dense attention and the fused-epilogue FFN GEMMs
+(bias+GELU, bias+residual, GELU backward; dim = heads * head_dim, hidden
+4 * dim) for one
 sequence of the chosen shape (default: stack_100m, 8192 tokens, 16 heads of
 64). ``--once`` runs every op exactly once (forward and backward) and
 prints a marker after each: the small, short-lived program to put under a
@@ -73,8 +75,23 @@ def main(argv=None):
     def gated_fwd_bwd():
         return torch.autograd.grad(dense_attention(q, k, v, pos, b, "cuda"), (q, k, v), g_gated)
 
+    from ..ops import gemm as G
+    dim = H * D
+    ffn = torch.nn.Sequential(torch.nn.Linear(dim, 4 * dim), torch.nn.GELU(), torch.nn.Linear(4 * dim, dim)).cuda()
+    h_in = torch.randn(1, n, dim, device="cuda").to(torch.bfloat16).requires_grad_()
+    y_in = torch.randn(1, n, dim, device="cuda", requires_grad=True)
+    g_ffn = torch.randn(1, n, dim, device="cuda")
+
+    def ffn_fwd():
+        with torch.no_grad():
+            return G.FFNResidual.apply(h_in, y_in, ffn[0].weight, ffn[0].bias, ffn[2].weight, ffn[2].bias)
+
+    def ffn_fwd_bwd():
+        out = G.FFNResidual.apply(h_in, y_in, ffn[0].weight, ffn[0].bias, ffn[2].weight, ffn[2].bias)
+        return torch.autograd.grad(out, (h_in, y_in, ffn[0].weight, ffn[2].weight), g_ffn)
+
     ops = {"local_fwd": local_fwd, "local_fwd_bwd": local_fwd_bwd, "gated_fwd": gated_fwd,
-           "gated_fwd_bwd": gated_fwd_bwd}
+           "gated_fwd_bwd": gated_fwd_bwd, "ffn_fwd": ffn_fwd, "ffn_fwd_bwd": ffn_fwd_bwd}
     if args.once:
         for name, fn in ops.items():
             fn()
