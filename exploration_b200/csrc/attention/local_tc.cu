@@ -87,8 +87,13 @@ EB_DEVICE void rotate_tile(__nv_bfloat16* tile, int rows, int off0, const float*
     uint4 a = *lo, b = *hi;
     __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
     __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&b);
-    const float* cs = cos_t + (r + off0) * 32 + 8 * c;
-    const float* sn = sin_t + (r + off0) * 32 + 8 * c;
+    // Table rows are 128 bytes and the 8 angles of chunk c start 32 bytes in:
+    // two 16-byte loads each for cos and sin.
+    const float4* cs4 = reinterpret_cast<const float4*>(cos_t + (r + off0) * 32 + 8 * c);
+    const float4* sn4 = reinterpret_cast<const float4*>(sin_t + (r + off0) * 32 + 8 * c);
+    const float4 ca = __ldg(cs4), cb = __ldg(cs4 + 1), sa = __ldg(sn4), sb = __ldg(sn4 + 1);
+    const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+    const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 x1 = __bfloat1622float2(pa[i]), x2 = __bfloat1622float2(pb[i]);
@@ -173,13 +178,11 @@ local_tc_fwd_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
     const int tid = threadIdx.x - 128;
     const int w = warp - 4;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
-    // 1. Rotate Q (offsets 16..143) and K (0..143) in place.
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull) &&
-                                          mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
-    if (ok) {
-      rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
-      rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
-    }
+    // 1. Rotate Q (offsets 16..143) as soon as it lands, then K (0..143), in place.
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
+    if (ok) rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+    if (ok) rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     // 2. Softmax of row r over its window: keys 16 * (r / 16) .. + 31 (CTA key index).
@@ -321,13 +324,19 @@ EB_DEVICE bool bwd_key_ok(const LtBwdArgs& a, int t) {
 
 // RoPE backward on a 64-wide fp32 row held as 64 values: x = R(-theta) y.
 EB_DEVICE void unrotate_row(float (&y)[64], int offset, const float* cos_t, const float* sin_t) {
-  const float* cs = cos_t + offset * 32;
-  const float* sn = sin_t + offset * 32;
+  const float4* cs = reinterpret_cast<const float4*>(cos_t + offset * 32);    // 128-byte table rows
+  const float4* sn = reinterpret_cast<const float4*>(sin_t + offset * 32);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float a = y[i], b = y[i + 32], c = cs[i], s = sn[i];
-    y[i] = a * c + b * s;
-    y[i + 32] = b * c - a * s;
+  for (int i4 = 0; i4 < 8; ++i4) {
+    const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+    const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = 4 * i4 + j;
+      const float a = y[i], b = y[i + 32];
+      y[i] = a * cc[j] + b * ss[j];
+      y[i + 32] = b * cc[j] - a * ss[j];
+    }
   }
 }
 
@@ -470,12 +479,10 @@ local_tc_dq_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_cons
     const int tid = threadIdx.x - 128;
     const int w = warp - 4;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull) &&
-                                          mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
-    if (ok) {
-      rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
-      rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
-    }
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
+    if (ok) rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+    if (ok) rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     // Row statistics: lse (base 2) and delta = dO . O (stored for the key kernel).
@@ -691,13 +698,11 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
     const int tid = threadIdx.x - 128;
     const int w = warp - 4;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull) &&
-                                          mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
-    if (ok) {
-      // Origin 16 rows before s0: key row k at offset k + 16, query row i at i + 16.
-      rotate_tile(sm.k, kM, kB, a.cos, a.sin, tid, 128);
-      rotate_tile(sm.q, kKeys, kB, a.cos, a.sin, tid, 128);
-    }
+    // Origin 16 rows before s0: key row k at offset k + 16, query row i at i + 16.
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+    if (ok) rotate_tile(sm.k, kM, kB, a.cos, a.sin, tid, 128);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
+    if (ok) rotate_tile(sm.q, kKeys, kB, a.cos, a.sin, tid, 128);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     const int kr = tid, tk = s0 + kr;              // key row and token
