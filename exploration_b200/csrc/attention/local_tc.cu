@@ -74,39 +74,61 @@ EB_DEVICE bool key_ok(const LtArgs& a, int t) {
   return t < a.n && a.start + t >= a.valid_start;
 }
 
-// Rotate rows [0, rows) of a 64-wide bf16 tile stored with the 128-byte
+// Rotate rows [0, ROWS) of a 64-wide bf16 tile stored with the 128-byte
 // swizzle (row r at r * 128 bytes, 16-byte chunk c at chunk c ^ (r & 7)) by
-// the RoPE angle of offset (r + off0): dims d and d + 32 form a pair.
-EB_DEVICE void rotate_tile(__nv_bfloat16* tile, int rows, int off0, const float* cos_t, const float* sin_t,
-                           int tid, int nthreads) {
+// the RoPE angle of offset (r + off0): dims d and d + 32 form a pair. 128
+// threads; thread tid always owns chunk c = tid & 3 of rows r0 + 32 k
+// (r0 = tid / 4), so it reads the table twice, for its first row and for the
+// 32-row step, and advances by the angle-addition formulas
+//   cos(a + b) = cos a cos b - sin a sin b,  sin(a + b) = sin a cos b + cos a sin b
+// (at most four steps of fp32 rounding, far below the bf16 output).
+template <int ROWS>
+EB_DEVICE void rotate_tile(__nv_bfloat16* tile, int off0, const float* cos_t, const float* sin_t, int tid) {
+  constexpr int kPer = (ROWS * 4 + 127) / 128;
   uint8_t* base = reinterpret_cast<uint8_t*>(tile);
-  for (int item = tid; item < rows * 4; item += nthreads) {
-    const int r = item >> 2, c = item & 3;
-    uint4* lo = reinterpret_cast<uint4*>(base + r * 128 + ((c ^ (r & 7)) << 4));
-    uint4* hi = reinterpret_cast<uint4*>(base + r * 128 + (((c + 4) ^ (r & 7)) << 4));
-    uint4 a = *lo, b = *hi;
-    __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
-    __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&b);
-    // Table rows are 128 bytes and the 8 angles of chunk c start 32 bytes in:
-    // two 16-byte loads each for cos and sin.
-    const float4* cs4 = reinterpret_cast<const float4*>(cos_t + (r + off0) * 32 + 8 * c);
-    const float4* sn4 = reinterpret_cast<const float4*>(sin_t + (r + off0) * 32 + 8 * c);
-    const float4 ca = __ldg(cs4), cb = __ldg(cs4 + 1), sa = __ldg(sn4), sb = __ldg(sn4 + 1);
-    const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-    const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+  const int r0 = tid >> 2, c = tid & 3;
+  // Table rows are 128 bytes and the 8 angles of chunk c start 32 bytes in.
+  const float4* c0p = reinterpret_cast<const float4*>(cos_t + (r0 + off0) * 32 + 8 * c);
+  const float4* s0p = reinterpret_cast<const float4*>(sin_t + (r0 + off0) * 32 + 8 * c);
+  const float4* cdp = reinterpret_cast<const float4*>(cos_t + 32 * 32 + 8 * c);
+  const float4* sdp = reinterpret_cast<const float4*>(sin_t + 32 * 32 + 8 * c);
+  const float4 c0a = __ldg(c0p), c0b = __ldg(c0p + 1), s0a = __ldg(s0p), s0b = __ldg(s0p + 1);
+  const float4 cda = __ldg(cdp), cdb = __ldg(cdp + 1), sda = __ldg(sdp), sdb = __ldg(sdp + 1);
+  float cs[8] = {c0a.x, c0a.y, c0a.z, c0a.w, c0b.x, c0b.y, c0b.z, c0b.w};
+  float sn[8] = {s0a.x, s0a.y, s0a.z, s0a.w, s0b.x, s0b.y, s0b.z, s0b.w};
+  const float cd[8] = {cda.x, cda.y, cda.z, cda.w, cdb.x, cdb.y, cdb.z, cdb.w};
+  const float sd[8] = {sda.x, sda.y, sda.z, sda.w, sdb.x, sdb.y, sdb.z, sdb.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 x1 = __bfloat1622float2(pa[i]), x2 = __bfloat1622float2(pb[i]);
-      const float c0 = cs[2 * i], c1 = cs[2 * i + 1], s0 = sn[2 * i], s1 = sn[2 * i + 1];
-      pa[i] = __floats2bfloat162_rn(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
-      pb[i] = __floats2bfloat162_rn(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+  for (int k = 0; k < kPer; ++k) {
+    const int r = r0 + 32 * k;
+    if (r < ROWS) {
+      uint4* lo = reinterpret_cast<uint4*>(base + r * 128 + ((c ^ (r & 7)) << 4));
+      uint4* hi = reinterpret_cast<uint4*>(base + r * 128 + (((c + 4) ^ (r & 7)) << 4));
+      uint4 xa = *lo, xb = *hi;
+      __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&xa);
+      __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&xb);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 x1 = __bfloat1622float2(pa[i]), x2 = __bfloat1622float2(pb[i]);
+        const float ca = cs[2 * i], cb = cs[2 * i + 1], sa = sn[2 * i], sb = sn[2 * i + 1];
+        pa[i] = __floats2bfloat162_rn(x1.x * ca - x2.x * sa, x1.y * cb - x2.y * sb);
+        pb[i] = __floats2bfloat162_rn(x2.x * ca + x1.x * sa, x2.y * cb + x1.y * sb);
+      }
+      *lo = xa;
+      *hi = xb;
     }
-    *lo = a;
-    *hi = b;
+    if (k + 1 < kPer) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float cn = cs[j] * cd[j] - sn[j] * sd[j];
+        sn[j] = sn[j] * cd[j] + cs[j] * sd[j];
+        cs[j] = cn;
+      }
+    }
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 local_tc_fwd_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
                     const __grid_constant__ CUtensorMap t_prev, LtArgs a) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
@@ -180,9 +202,9 @@ local_tc_fwd_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
     // 1. Rotate Q (offsets 16..143) as soon as it lands, then K (0..143), in place.
     bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
-    if (ok) rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
+    if (ok) rotate_tile<kM>(sm.q, kB, a.cos, a.sin, tid);
     ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
-    if (ok) rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
+    if (ok) rotate_tile<kKeys>(sm.k, 0, a.cos, a.sin, tid);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     // 2. Softmax of row r over its window: keys 16 * (r / 16) .. + 31 (CTA key index).
@@ -390,7 +412,7 @@ EB_DEVICE void store_band_bf16(uint32_t addr, int w, const float (&x)[48]) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 local_tc_dq_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
                    const __grid_constant__ CUtensorMap t_prev, const __grid_constant__ CUtensorMap t_dout,
                    LtBwdArgs a) {
@@ -480,9 +502,9 @@ local_tc_dq_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_cons
     const int w = warp - 4;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
     bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
-    if (ok) rotate_tile(sm.q, kM, kB, a.cos, a.sin, tid, 128);
+    if (ok) rotate_tile<kM>(sm.q, kB, a.cos, a.sin, tid);
     ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
-    if (ok) rotate_tile(sm.k, kKeys, 0, a.cos, a.sin, tid, 128);
+    if (ok) rotate_tile<kKeys>(sm.k, 0, a.cos, a.sin, tid);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     // Row statistics: lse (base 2) and delta = dO . O (stored for the key kernel).
@@ -700,9 +722,9 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
     // Origin 16 rows before s0: key row k at offset k + 16, query row i at i + 16.
     bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
-    if (ok) rotate_tile(sm.k, kM, kB, a.cos, a.sin, tid, 128);
+    if (ok) rotate_tile<kM>(sm.k, kB, a.cos, a.sin, tid);
     ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
-    if (ok) rotate_tile(sm.q, kKeys, kB, a.cos, a.sin, tid, 128);
+    if (ok) rotate_tile<kKeys>(sm.q, kB, a.cos, a.sin, tid);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     const int kr = tid, tk = s0 + kr;              // key row and token

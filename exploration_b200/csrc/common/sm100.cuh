@@ -77,13 +77,15 @@ EB_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: about a second at most. Returns false (and reports) on timeout
-// or when the CTA already aborted.
+// or when the CTA already aborted. With site == kSiteDrain (an aborted CTA
+// waiting for its own copies in flight before it exits) the abort flag is
+// ignored and only the time bound applies.
 EB_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, ErrorSlot* err, int site) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   const long long limit = 2000000000LL;   // ~1 s at 1.9 GHz
   while (true) {
-    if (*abort) return false;
+    if (site != kSiteDrain && *abort) return false;
     if (mbar_try_wait(bar, parity)) return true;
     if (clock64() - start > limit) {
       *abort = 1;
