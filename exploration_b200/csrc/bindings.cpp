@@ -19,7 +19,9 @@ long long launch_count();
 std::vector<at::Tensor> layer_norm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, double eps,
                                        at::ScalarType out_dtype);
 std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                       const at::Tensor& mean, const at::Tensor& rstd);
+                                       const at::Tensor& mean, const at::Tensor& rstd,
+                                       const c10::optional<at::Tensor>& dres, const c10::optional<at::Tensor>& dw_acc,
+                                       const c10::optional<at::Tensor>& db_acc);
 at::Tensor bias_gelu_fwd(const at::Tensor& h, const at::Tensor& bias);
 std::vector<at::Tensor> bias_gelu_bwd(const at::Tensor& dout, const at::Tensor& h, const at::Tensor& bias);
 std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets);
@@ -110,7 +112,9 @@ std::pair<int, int> device_errors(int device) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "exploration_b200 sm_100a kernels";
   m.def("layer_norm_fwd", &eb::layer_norm_fwd);
-  m.def("layer_norm_bwd", &eb::layer_norm_bwd);
+  m.def("layer_norm_bwd", &eb::layer_norm_bwd, "LayerNorm backward; optional residual-gradient add and "
+        "accumulation into parameter gradients", py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"),
+        py::arg("rstd"), py::arg("dres") = py::none(), py::arg("dw_acc") = py::none(), py::arg("db_acc") = py::none());
   m.def("bias_gelu_fwd", &eb::bias_gelu_fwd);
   m.def("bias_gelu_bwd", &eb::bias_gelu_bwd);
   m.def("cross_entropy_fwd", &eb::cross_entropy_fwd);

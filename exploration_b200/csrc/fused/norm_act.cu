@@ -188,7 +188,7 @@ template <typename TIn, typename TGrad, int V>
 __global__ void __launch_bounds__(kVecWarps * 32)
 ln_bwd_vec_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
                   const float* __restrict__ mean, const float* __restrict__ rstd, TIn* __restrict__ dx,
-                  float* __restrict__ part_w, float* __restrict__ part_b, int rows) {
+                  float* __restrict__ part_w, float* __restrict__ part_b, int rows, const float* __restrict__ dres) {
   constexpr int cols = 128 * V;
   extern __shared__ float red[];                       // [kVecWarps][2][cols], then w [cols]
   float* ws = red + kVecWarps * 2 * cols;
@@ -233,6 +233,13 @@ ln_bwd_vec_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x, const
       float o[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) o[t] = rs * (dv[j][t] * wt[t] - s1 - xh[j][t] * s2);
+      if (dres != nullptr) {                             // the residual branch's gradient of x
+        const float4 r4 = *reinterpret_cast<const float4*>(dres + base + 128 * j + 4 * lane);
+        o[0] += r4.x;
+        o[1] += r4.y;
+        o[2] += r4.z;
+        o[3] += r4.w;
+      }
       store4<TIn>(dx + base + 128 * j + 4 * lane, o);
     }
   }
@@ -257,9 +264,11 @@ ln_bwd_vec_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x, const
   }
 }
 
-// out_w[c] = sum_s part_w[s][c], out_b likewise (one launch for both).
+// out_w[c] (+)= sum_s part_w[s][c], out_b likewise (one launch for both;
+// `accumulate` adds into the outputs, e.g. straight into parameter gradients).
 __global__ void column_sum2_kernel(const float* __restrict__ part_w, const float* __restrict__ part_b,
-                                   float* __restrict__ out_w, float* __restrict__ out_b, int splits, int cols) {
+                                   float* __restrict__ out_w, float* __restrict__ out_b, int splits, int cols,
+                                   int accumulate = 0) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   float aw = 0.f, ab = 0.f;
@@ -267,8 +276,8 @@ __global__ void column_sum2_kernel(const float* __restrict__ part_w, const float
     aw += part_w[static_cast<int64_t>(s) * cols + c];
     ab += part_b[static_cast<int64_t>(s) * cols + c];
   }
-  out_w[c] = aw;
-  out_b[c] = ab;
+  out_w[c] = accumulate ? out_w[c] + aw : aw;
+  out_b[c] = accumulate ? out_b[c] + ab : ab;
 }
 
 #define EB_DISPATCH_V(V_VALUE, NAME, ...)                                   \
@@ -394,14 +403,30 @@ std::vector<at::Tensor> layer_norm_fwd(const at::Tensor& x, const at::Tensor& w,
   return {y, mean, rstd};
 }
 
+// dres: optional fp32 gradient of x from another branch, added to dx inside the
+// kernel. dw_acc / db_acc: optional fp32 [cols] tensors (parameter gradients)
+// the weight and bias gradients are added into instead of being returned fresh.
 std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                       const at::Tensor& mean, const at::Tensor& rstd) {
+                                       const at::Tensor& mean, const at::Tensor& rstd,
+                                       const c10::optional<at::Tensor>& dres_opt,
+                                       const c10::optional<at::Tensor>& dw_acc,
+                                       const c10::optional<at::Tensor>& db_acc) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.sizes() == x.sizes(), "dy/x mismatch");
   const c10::cuda::CUDAGuard guard(x.device());
   const int rows = x.size(0), cols = x.size(1);
+  const bool has_res = dres_opt.has_value() && dres_opt->defined();
+  if (has_res)
+    TORCH_CHECK(dres_opt->is_contiguous() && dres_opt->scalar_type() == at::kFloat && dres_opt->numel() == x.numel(),
+                "layer_norm_bwd: dres must be contiguous fp32 with x's size");
+  const bool acc = dw_acc.has_value() && dw_acc->defined();
+  if (acc)
+    TORCH_CHECK(db_acc.has_value() && db_acc->defined() && dw_acc->is_contiguous() && db_acc->is_contiguous() &&
+                    dw_acc->scalar_type() == at::kFloat && db_acc->scalar_type() == at::kFloat &&
+                    dw_acc->numel() == cols && db_acc->numel() == cols,
+                "layer_norm_bwd: dw_acc/db_acc must be contiguous fp32 [cols]");
   auto dx = at::empty_like(x);
-  auto dw = at::zeros({cols}, x.options().dtype(at::kFloat));
-  auto db = at::zeros({cols}, x.options().dtype(at::kFloat));
+  at::Tensor dw = acc ? *dw_acc : at::zeros({cols}, x.options().dtype(at::kFloat));
+  at::Tensor db = acc ? *db_acc : at::zeros({cols}, x.options().dtype(at::kFloat));
   if (rows == 0) return {dx, dw, db};
   auto stream = at::cuda::getCurrentCUDAStream();
   if (vec_width(cols) && cols <= 1024) {
@@ -417,12 +442,14 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
           kernel<<<ctas, kVecWarps * 32, smem, stream>>>(
               reinterpret_cast<const TGrad*>(dy.data_ptr()), reinterpret_cast<const TIn*>(x.data_ptr()),
               w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
-              reinterpret_cast<TIn*>(dx.data_ptr()), pw.data_ptr<float>(), pb.data_ptr<float>(), rows);
+              reinterpret_cast<TIn*>(dx.data_ptr()), pw.data_ptr<float>(), pb.data_ptr<float>(), rows,
+              has_res ? dres_opt->data_ptr<float>() : nullptr);
         });
       });
     });
     column_sum2_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(pw.data_ptr<float>(), pb.data_ptr<float>(),
-                                                           dw.data_ptr<float>(), db.data_ptr<float>(), ctas, cols);
+                                                           dw.data_ptr<float>(), db.data_ptr<float>(), ctas, cols,
+                                                           acc ? 1 : 0);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     count_launch(2);
     return {dx, dw, db};
@@ -444,12 +471,20 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
           part_b.data_ptr<float>(), rows, cols, per_split);
     });
   });
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_w.data_ptr<float>(), dw.data_ptr<float>(),
+  // General widths: fresh sums, then the optional accumulations as separate adds.
+  at::Tensor dw_f = acc ? at::empty({cols}, x.options().dtype(at::kFloat)) : dw;
+  at::Tensor db_f = acc ? at::empty({cols}, x.options().dtype(at::kFloat)) : db;
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_w.data_ptr<float>(), dw_f.data_ptr<float>(),
                                                          splits, cols);
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_b.data_ptr<float>(), db.data_ptr<float>(),
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_b.data_ptr<float>(), db_f.data_ptr<float>(),
                                                          splits, cols);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(4);
+  if (acc) {
+    dw.add_(dw_f);
+    db.add_(db_f);
+  }
+  if (has_res) dx.add_(dres_opt->view(dx.sizes()));
   return {dx, dw, db};
 }
 

@@ -82,8 +82,8 @@ class HaloMemoryBlock(nn.Module):
         self.ffn_norm = nn.LayerNorm(dim)
         self.ffn = FeedForward(dim, ffn_ratio)
 
-    def _project(self, x):
-        return fused.linear(fused.layer_norm(x, self.attn_norm, self.backend), self.qkv, self.backend)
+    def _project(self, x, link=None):
+        return fused.linear(fused.layer_norm(x, self.attn_norm, self.backend, link), self.qkv, self.backend)
 
     def forward_chunk(self, x, previous=None, start=0):
         """Encode one block-aligned chunk given the previous layer-input block.
@@ -99,13 +99,16 @@ class HaloMemoryBlock(nn.Module):
         if previous is not None and tuple(previous.shape) != (batch, b, dim):
             raise ValueError("previous halo must contain exactly one block")
         valid_start = start if previous is None else max(0, start - b)
-        qkv = self._project(x).view(batch, n, 3, self.heads, self.hd)
+        # x and y each feed a LayerNorm and a residual add: the links let the
+        # LayerNorm backward add the residual branch's gradient in its kernel.
+        link_x, link_y = fused.ResidualLink(), fused.ResidualLink()
+        qkv = self._project(x, link_x).view(batch, n, 3, self.heads, self.hd)
         halo = None if previous is None else \
             self._project(previous).view(batch, b, 3, self.heads, self.hd)
         context = fused.local_attention(qkv, halo, start, valid_start, n, b, self.heads, self.backend)
-        y = fused.linear_residual(context, self.out, x, self.backend)
-        return fused.ffn_residual(fused.layer_norm(y, self.ffn_norm, self.backend), y, self.ffn,
-                                  self.backend)
+        y = fused.linear_residual(context, self.out, x, self.backend, link_x)
+        return fused.ffn_residual(fused.layer_norm(y, self.ffn_norm, self.backend, link_y), y, self.ffn,
+                                  self.backend, link_y)
 
     def chunk_tokens(self, x) -> int:
         step = self.query_chunk_size * self.block_size

@@ -189,20 +189,27 @@ class StackModel(nn.Module):
 
     # -- dense read round ----------------------------------------------------
 
-    def _query(self, rd, z):
-        return fused.linear(fused.layer_norm(z, rd.q_norm, self.backend), rd.wq, self.backend)
+    def _query(self, rd, z, link=None):
+        return fused.linear(fused.layer_norm(z, rd.q_norm, self.backend, link), rd.wq, self.backend)
 
-    def _finish(self, rd, z, context):
-        z = fused.linear_residual(context, rd.read_out, z, self.backend)
-        return fused.ffn_residual(fused.layer_norm(z, rd.ffn_norm, self.backend), z, rd.ffn,
-                                  self.backend)
+    def _finish(self, rd, z, context, link=None):
+        z = fused.linear_residual(context, rd.read_out, z, self.backend, link)
+        return self._ffn(rd, z)
+
+    def _ffn(self, rd, z):
+        link = fused.ResidualLink()       # z feeds ffn_norm and the FFN residual
+        return fused.ffn_residual(fused.layer_norm(z, rd.ffn_norm, self.backend, link), z, rd.ffn,
+                                  self.backend, link)
 
     def _dense_round(self, rd, z, k, v, positions, parallel):
         recompute = self.checkpoint_chunks and torch.is_grad_enabled()
         if not recompute and parallel.ulysses is not None and self._native(z):
-            h = fused.layer_norm(z, rd.q_norm, self.backend)
+            link = fused.ResidualLink()   # z feeds q_norm and the read_out residual
+            h = fused.layer_norm(z, rd.q_norm, self.backend, link)
             fused_exchange = parallel.fused(h, self.heads, self.hd)
-            if fused_exchange is not None:
+            if fused_exchange is None:
+                link.armed = False        # h is dropped: the residual op keeps its gradient
+            else:
                 # Query projection -> head owners, attention, then the output
                 # projection reading the context straight from its owners.
                 q = fused_exchange.project_to_heads(h, rd.wq.weight, 1, self.heads, self.hd)[0]
@@ -210,13 +217,13 @@ class StackModel(nn.Module):
                     k, v = k.to(q.dtype), v.to(q.dtype)
                 ctx = dense_attention(q, k, v, positions, self.block_size, self.backend,
                                       q_chunk=self.attention_q_chunk, kv_chunk=self.attention_kv_chunk)
-                z = fused_exchange.heads_to_linear_residual(ctx, rd.read_out, z)
-                return fused.ffn_residual(fused.layer_norm(z, rd.ffn_norm, self.backend), z, rd.ffn,
-                                          self.backend)
+                z = fused_exchange.heads_to_linear_residual(ctx, rd.read_out, z, link)
+                return self._ffn(rd, z)
+        link = fused.ResidualLink()       # z feeds q_norm and the read_out residual
         if recompute:
-            q = checkpoint(self._query, rd, z, use_reentrant=False, preserve_rng_state=False)
+            q = checkpoint(self._query, rd, z, link, use_reentrant=False, preserve_rng_state=False)
         else:
-            q = self._query(rd, z)
+            q = self._query(rd, z, link)
         q = parallel.to_heads(q.reshape(*z.shape[:2], self.heads, self.hd))
         if k.dtype != q.dtype:
             k, v = k.to(q.dtype), v.to(q.dtype)
@@ -224,8 +231,8 @@ class StackModel(nn.Module):
                               q_chunk=self.attention_q_chunk, kv_chunk=self.attention_kv_chunk)
         ctx = parallel.to_sequence(ctx).reshape(*z.shape[:2], self.dim)
         if recompute:
-            return checkpoint(self._finish, rd, z, ctx, use_reentrant=False, preserve_rng_state=False)
-        return self._finish(rd, z, ctx)
+            return checkpoint(self._finish, rd, z, ctx, link, use_reentrant=False, preserve_rng_state=False)
+        return self._finish(rd, z, ctx, link)
 
     def _head_loss(self, hidden, labels):
         h = fused.layer_norm(hidden, self.final_norm, self.backend)

@@ -106,15 +106,54 @@ def clear_cast_cache() -> None:
 # ----------------------------------------------------------------------------
 
 
+class ResidualLink:
+    """Pairs the LayerNorm and the residual op that read one residual-stream tensor.
+
+    ``x`` feeds both ``LayerNorm(x)`` (whose output leads, through the block,
+    to the residual op's other input) and the residual op itself
+    (``x + f(...)``), so autograd would add the two gradients of ``x`` in a
+    separate pass. With a link the residual op's backward leaves its
+    gradient here instead of returning it, and the LayerNorm backward, which
+    always runs later, adds it to ``dx`` inside the kernel. The LayerNorm
+    arms the link in its forward; a residual op that finds the link unarmed
+    (no native LayerNorm on the other branch) returns its gradient normally.
+    """
+
+    __slots__ = ("armed", "grad")
+
+    def __init__(self):
+        self.armed = False
+        self.grad = None
+
+    def take(self):
+        grad, self.grad = self.grad, None
+        return grad
+
+
+def _sink_grad(param):
+    """``param.grad`` if gradients of ``param`` are accumulated in place (a registered sink)."""
+    sink = gemm._grad_sinks.get(id(param))
+    if sink is None or sink[0]() is not param:
+        return None, None
+    grad = param.grad
+    if grad is None or grad.dtype != torch.float32 or not grad.is_contiguous():
+        return None, None
+    return grad, sink[1]
+
+
 class _LayerNormNative(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, bias, eps, out_dtype):
+    def forward(ctx, x, weight, bias, eps, out_dtype, link):
         ext = _native.native(x)
         flat = x.reshape(-1, x.shape[-1]).contiguous()
         y, mean, rstd = ext.layer_norm_fwd(flat, weight, bias, eps, out_dtype)
         record("layer_norm_fwd", width=x.shape[-1], in_dtype=str(x.dtype), out_dtype=str(out_dtype))
         ctx.save_for_backward(flat, weight, mean, rstd)
+        ctx.params = (weight, bias)
         ctx.shape = x.shape
+        ctx.link = link
+        if link is not None:
+            link.armed = True
         return y.view(*x.shape[:-1], y.shape[-1])
 
     @staticmethod
@@ -122,20 +161,37 @@ class _LayerNormNative(torch.autograd.Function):
     def backward(ctx, grad):
         flat, weight, mean, rstd = ctx.saved_tensors
         ext = _native.native(flat)
-        dx, dw, db = ext.layer_norm_bwd(grad.reshape(flat.shape).contiguous(), flat, weight, mean, rstd)
-        return dx.view(ctx.shape), dw, db, None, None
+        dres = ctx.link.take() if ctx.link is not None else None
+        if dres is not None:
+            dres = dres.reshape(flat.shape)
+            if dres.dtype != torch.float32 or not dres.is_contiguous():
+                dres = dres.float().contiguous()
+        w_acc, w_done = _sink_grad(ctx.params[0])
+        b_acc, b_done = _sink_grad(ctx.params[1])
+        if w_acc is None or b_acc is None:
+            w_acc = b_acc = None
+        dx, dw, db = ext.layer_norm_bwd(grad.reshape(flat.shape).contiguous(), flat, weight, mean, rstd,
+                                        dres, w_acc, b_acc)
+        if w_acc is not None:
+            # Added into the parameters' gradients in place: report them complete.
+            w_done(ctx.params[0])
+            b_done(ctx.params[1])
+            return dx.view(ctx.shape), None, None, None, None, None
+        return dx.view(ctx.shape), dw, db, None, None, None
 
 
 def _fp32(t):
     return t if t is None or t.dtype == torch.float32 else t.float()
 
 
-def layer_norm(x, norm: torch.nn.LayerNorm, backend: str = "auto"):
-    """``norm(x)``; on CUDA the output is already in the matmul dtype."""
+def layer_norm(x, norm: torch.nn.LayerNorm, backend: str = "auto", link: ResidualLink | None = None):
+    """``norm(x)``; on CUDA the output is already in the matmul dtype.
+
+    ``link``: the residual op that also reads ``x`` (see :class:`ResidualLink`)."""
     cdt = compute_dtype(x, norm.weight.dtype)
     if use_native(x, backend, cdt) and x.dtype in (torch.float32, torch.bfloat16):
         # The kernels read fp32 affine parameters (a bf16-cast model passes copies).
-        return _LayerNormNative.apply(x, _fp32(norm.weight), _fp32(norm.bias), norm.eps, cdt)
+        return _LayerNormNative.apply(x, _fp32(norm.weight), _fp32(norm.bias), norm.eps, cdt, link)
     return F.layer_norm(x, norm.normalized_shape, norm.weight, norm.bias, norm.eps)
 
 
@@ -158,22 +214,23 @@ def linear(x, layer: torch.nn.Linear, backend: str = "auto", out_f32: bool = Fal
     return out.float() if out_f32 else out
 
 
-def linear_residual(x, layer: torch.nn.Linear, residual, backend: str = "auto"):
+def linear_residual(x, layer: torch.nn.Linear, residual, backend: str = "auto", link: ResidualLink | None = None):
     """``residual + layer(x)``; on the native path one GEMM whose epilogue adds the fp32 residual."""
     cdt = compute_dtype(x, layer.weight.dtype)
     if use_native(x, backend, cdt) and cdt == torch.bfloat16 and residual.dtype == torch.float32 \
             and gemm.usable(x.to(cdt), layer):
-        return gemm.LinearResidual.apply(x.to(cdt), layer.weight, _fp32(layer.bias), residual)
+        return gemm.LinearResidual.apply(x.to(cdt), layer.weight, _fp32(layer.bias), residual, link)
     return residual + linear(x, layer, backend)
 
 
-def ffn_residual(h, y, ffn: torch.nn.Sequential, backend: str = "auto"):
+def ffn_residual(h, y, ffn: torch.nn.Sequential, backend: str = "auto", link: ResidualLink | None = None):
     """``y + ffn(h)``: two GEMMs with bias+GELU and bias+residual epilogues when native."""
     up, down = ffn[0], ffn[2]
     cdt = compute_dtype(h, up.weight.dtype)
     if use_native(h, backend, cdt) and cdt == torch.bfloat16 and y.dtype == torch.float32 \
             and gemm.usable(h.to(cdt), up, down):
-        return gemm.FFNResidual.apply(h.to(cdt), y, up.weight, _fp32(up.bias), down.weight, _fp32(down.bias))
+        return gemm.FFNResidual.apply(h.to(cdt), y, up.weight, _fp32(up.bias), down.weight, _fp32(down.bias),
+                                      link)
     return y + feed_forward(h, ffn, backend)
 
 

@@ -87,6 +87,14 @@ def accumulate_weight_grad(param, g, x):
     return weight_grad(g, x)
 
 
+def hand_residual(link, dout):
+    """The residual input's gradient: left on the link for the paired LayerNorm, or returned."""
+    if link is None:
+        return dout
+    link.grad = dout
+    return None
+
+
 def _bf16_weight(param):
     from .fused import _cached_copy
     return _cached_copy(param, torch.bfloat16)
@@ -124,7 +132,7 @@ class LinearResidual(torch.autograd.Function):
     """``out = residual + x W^T (+ bias)`` in fp32."""
 
     @staticmethod
-    def forward(ctx, x, weight, bias, residual):
+    def forward(ctx, x, weight, bias, residual, link=None):
         x2 = _flat(x)
         w = _bf16_weight(weight)
         res = residual.reshape(-1, residual.shape[-1]).contiguous()
@@ -134,6 +142,7 @@ class LinearResidual(torch.autograd.Function):
         ctx.param = weight
         ctx.has_bias = bias is not None
         ctx.shape = x.shape
+        ctx.link = link if link is not None and link.armed else None
         return out.view(residual.shape)
 
     @staticmethod
@@ -145,14 +154,14 @@ class LinearResidual(torch.autograd.Function):
         dx = g @ w
         dw = accumulate_weight_grad(ctx.param, g, x2)
         db = d32.sum(0) if ctx.has_bias else None
-        return dx.view(ctx.shape), dw, db, dout
+        return dx.view(ctx.shape), dw, db, hand_residual(ctx.link, dout), None
 
 
 class FFNResidual(torch.autograd.Function):
     """``out = y + W2 gelu(W1 h + b1) + b2`` (fp32 out, bf16 GEMMs)."""
 
     @staticmethod
-    def forward(ctx, h, y, w1, b1, w2, b2):
+    def forward(ctx, h, y, w1, b1, w2, b2, link=None):
         h2 = _flat(h)
         y2 = y.reshape(-1, y.shape[-1]).contiguous()
         w1b, w2b = _bf16_weight(w1), _bf16_weight(w2)
@@ -165,6 +174,7 @@ class FFNResidual(torch.autograd.Function):
         ctx.save_for_backward(h2, dgelu, u, w1b, w2b)
         ctx.params = (w1, w2)
         ctx.shape = h.shape
+        ctx.link = link if link is not None and link.armed else None
         return out.view(y.shape)
 
     @staticmethod
@@ -181,7 +191,7 @@ class FFNResidual(torch.autograd.Function):
         db1 = partial.sum(0)
         dw1 = accumulate_weight_grad(ctx.params[0], dh_pre, h2)
         dh = dh_pre @ w1b
-        return dh.view(ctx.shape), dout, dw1, db1, dw2, db2
+        return dh.view(ctx.shape), hand_residual(ctx.link, dout), dw1, db1, dw2, db2, None
 
 
 def usable(x, *layers) -> bool:

@@ -78,7 +78,7 @@ class _ProjectToHeads(torch.autograd.Function):
 
 class _HeadsToLinearResidual(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, heads, weight, bias, residual, U):
+    def forward(ctx, heads, weight, bias, residual, U, link=None):
         heap = U.heap
         batch, n_total, hpr, hd = heads.shape
         n_local, C = n_total // U.world, hpr * hd
@@ -94,6 +94,7 @@ class _HeadsToLinearResidual(torch.autograd.Function):
                           G.BIAS_RESIDUAL, bias, res)
         ctx.save_for_backward(w)
         ctx.param = weight
+        ctx.link = link if link is not None and link.armed else None
         ctx.meta = (U, slot, batch, n_local, hpr, hd, bias is not None)
         return out.view(residual.shape)
 
@@ -115,7 +116,7 @@ class _HeadsToLinearResidual(torch.autograd.Function):
         U.ext.gather_rows(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, ctx_seq)
         dw = G.accumulate_weight_grad(ctx.param, g, ctx_seq)
         db = d32.sum(0) if has_bias else None
-        return dheads, dw, db, dout, None
+        return dheads, dw, db, G.hand_residual(ctx.link, dout), None, None
 
 
 class UlyssesFused:
@@ -143,10 +144,10 @@ class UlyssesFused:
         """``x [B, n_local, K]`` -> ``[parts, B, world * n_local, heads / world, head_dim]``."""
         return _ProjectToHeads.apply(x, weight, self, parts, heads // self.world, head_dim)
 
-    def heads_to_linear_residual(self, heads, layer, residual):
+    def heads_to_linear_residual(self, heads, layer, residual, link=None):
         """``residual + to_sequence(heads) W^T + b`` (fp32) for this rank's shard."""
         bias = layer.bias if layer.bias is None or layer.bias.dtype == torch.float32 else layer.bias.float()
-        return _HeadsToLinearResidual.apply(heads, layer.weight, bias, residual, self)
+        return _HeadsToLinearResidual.apply(heads, layer.weight, bias, residual, self, link)
 
     # Generic exchanges (no projection to fuse with) stay on the collective path.
     def to_heads(self, x):

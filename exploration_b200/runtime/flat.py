@@ -62,6 +62,8 @@ class FlatParameters:
         that group (collective), so peer kernels can reach every rank's copy."""
         params = [p for p in model.parameters() if p.requires_grad]
         fp32_read = {id(m.weight) for m in model.modules() if isinstance(m, torch.nn.Embedding)}
+        norm_ids = {id(t) for m in model.modules() if isinstance(m, torch.nn.LayerNorm)
+                    for t in (m.weight, m.bias) if t is not None}
         small = [p for p in params if p.dim() < 2 or id(p) in fp32_read]
         big = [p for p in params if not (p.dim() < 2 or id(p) in fp32_read)]
         self.params = small + big
@@ -74,6 +76,7 @@ class FlatParameters:
             total += -(-p.numel() // ALIGN) * ALIGN
         if not big:
             total = -(-total // quantum) * quantum
+        self.norm_ids = norm_ids
         self.split = offsets[len(small)] if big else total
         total = self.split + -(-(total - self.split) // quantum) * quantum
         self.total, self.offsets = total, offsets
@@ -104,6 +107,12 @@ class FlatParameters:
 
     def zero_grad(self) -> None:
         self.grad.zero_()
+
+    def sink_params(self):
+        """Parameters whose gradients the native ops add straight into ``param.grad``: the
+        GEMM weights (sharded region) and the LayerNorm weights and biases."""
+        return [p for p, off in zip(self.params, self.offsets)
+                if (off >= self.split and p.dim() == 2) or id(p) in self.norm_ids]
 
     def release(self) -> None:
         for p in self.params:
@@ -213,9 +222,8 @@ class _BucketCountdown:
         self.bounds, self.owner = _bucket_bounds(flat, bucket_bytes, split_boundary)
         self.count = None                          # contributions per bucket, learned in the first step
         self.handles = [p.register_post_accumulate_grad_hook(self._hook) for p in flat.params]
-        for p, off in zip(flat.params, flat.offsets):
-            if off >= flat.split and p.dim() == 2:
-                G.register_grad_sink(p, self._hook)
+        for p in flat.sink_params():
+            G.register_grad_sink(p, self._hook)
         self.active = False
 
     def start(self) -> None:
@@ -579,10 +587,9 @@ class GraphTrainer:
                                    shadow_only=native_bf16, layout=layout)
         self.use_graph = use_graph and self.cuda
         if self.cuda and self.buckets is None:
-            # One process: GEMM weight gradients still go straight into the flat buffer.
-            for p, off in zip(self.flat.params, self.flat.offsets):
-                if off >= self.flat.split and p.dim() == 2:
-                    G.register_grad_sink(p, _no_signal)
+            # One process: GEMM weight and LayerNorm gradients still go straight into the flat buffer.
+            for p in self.flat.sink_params():
+                G.register_grad_sink(p, _no_signal)
         self.graph = None
         self.graph_launches = 0
         self.calls = 0
