@@ -210,7 +210,7 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "strong" if cp > 1 or world == 1 else "weak",
             "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
             "dtype": "bf16", "data": "synthetic (uniform random token ids), random-init weights",
-            "config": {"model": "stack_100m", "global_batch": parallel.dp_size, "seq_len": args.length,
+            "config": {"model": Path(args.config).stem, "global_batch": parallel.dp_size, "seq_len": args.length,
                        "parallelism": f"cp{cp}" + (f"xdp{parallel.dp_size}" if parallel.dp_size > 1 else ""),
                        "activation_recompute": bool(args.recompute), "optimizer": "fused AdamW fp32 master",
                        "l2": "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)",
@@ -267,7 +267,7 @@ def run_reference(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "strong" if cp > 1 or world == 1 else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform random token ids), random-init weights",
-            "config": {"model": "stack_100m", "global_batch": dp, "seq_len": args.length,
+            "config": {"model": Path(args.config).stem, "global_batch": dp, "seq_len": args.length,
                        "parallelism": f"cp{cp}", "activation_recompute": bool(args.recompute),
                        "timing": "reference's own per-step host clock after cuda.synchronize, max over ranks"},
             "peak_allocated_gib": train[-1].get("peak_allocated_gib") if train else None}
