@@ -23,6 +23,8 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
                                        const c10::optional<at::Tensor>& dres, const c10::optional<at::Tensor>& dw_acc,
                                        const c10::optional<at::Tensor>& db_acc);
 at::Tensor bias_gelu_fwd(const at::Tensor& h, const at::Tensor& bias);
+std::vector<at::Tensor> cast_colsum(const at::Tensor& x, const c10::optional<at::Tensor>& sum_acc);
+at::Tensor column_sum(const at::Tensor& part, const c10::optional<at::Tensor>& sum_acc);
 std::vector<at::Tensor> bias_gelu_bwd(const at::Tensor& dout, const at::Tensor& h, const at::Tensor& bias);
 std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets);
 void adamw_step(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
@@ -116,6 +118,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "accumulation into parameter gradients", py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"),
         py::arg("rstd"), py::arg("dres") = py::none(), py::arg("dw_acc") = py::none(), py::arg("db_acc") = py::none());
   m.def("bias_gelu_fwd", &eb::bias_gelu_fwd);
+  m.def("cast_colsum", &eb::cast_colsum, "fp32 -> (bf16 copy, column sums; optionally added into sum_acc)",
+        py::arg("x"), py::arg("sum_acc") = py::none());
+  m.def("column_sum", &eb::column_sum, "column sums of fp32 partials (optionally added into sum_acc)",
+        py::arg("part"), py::arg("sum_acc") = py::none());
   m.def("bias_gelu_bwd", &eb::bias_gelu_bwd);
   m.def("cross_entropy_fwd", &eb::cross_entropy_fwd);
   m.def("adamw_step", &eb::adamw_step);

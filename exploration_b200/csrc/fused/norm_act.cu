@@ -96,12 +96,37 @@ layer_norm_bwd_dwdb_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__
 }
 
 __global__ void column_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                  int splits, int cols) {
+                                  int splits, int cols, int accumulate = 0) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   float acc = 0.f;
   for (int s = 0; s < splits; ++s) acc += part[static_cast<int64_t>(s) * cols + c];
-  out[c] = acc;
+  out[c] = accumulate ? out[c] + acc : acc;
+}
+
+// Gradient of a linear layer's fp32 output: the bf16 copy the GEMMs read and
+// the per-CTA column sums (the bias gradient) in one read of the input.
+// CTA = kCastRows rows; thread = 4 consecutive columns (grid-stride over cols).
+constexpr int kCastRows = 32;
+
+__global__ void __launch_bounds__(256) cast_colsum_kernel(const float4* __restrict__ x, uint2* __restrict__ out,
+                                                          float4* __restrict__ part, int rows, int cols4) {
+  const int r0 = blockIdx.x * kCastRows, r1 = min(rows, r0 + kCastRows);
+  for (int c = threadIdx.x; c < cols4; c += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int r = r0; r < r1; ++r) {
+      const int64_t i = static_cast<int64_t>(r) * cols4 + c;
+      const float4 v = x[i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+      __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+      out[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
+    part[static_cast<int64_t>(blockIdx.x) * cols4 + c] = acc;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -486,6 +511,53 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
   }
   if (has_res) dx.add_(dres_opt->view(dx.sizes()));
   return {dx, dw, db};
+}
+
+// x fp32 [rows, cols] -> (bf16 copy, column sums). With `sum_acc` (fp32 [cols],
+// e.g. a bias gradient) the sums are added into it and it is returned.
+std::vector<at::Tensor> cast_colsum(const at::Tensor& x, const c10::optional<at::Tensor>& sum_acc) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 2 && x.scalar_type() == at::kFloat &&
+                  x.size(1) % 4 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "cast_colsum: contiguous 16-byte aligned fp32 [rows, cols], cols % 4 == 0");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rows = x.size(0), cols = x.size(1);
+  const bool acc = sum_acc.has_value() && sum_acc->defined();
+  if (acc)
+    TORCH_CHECK(sum_acc->is_contiguous() && sum_acc->scalar_type() == at::kFloat && sum_acc->numel() == cols,
+                "cast_colsum: sum_acc must be contiguous fp32 [cols]");
+  auto out = at::empty({rows, cols}, x.options().dtype(at::kBFloat16));
+  at::Tensor sums = acc ? *sum_acc : at::zeros({cols}, x.options());
+  if (rows == 0) return {out, sums};
+  const int ctas = cdiv(rows, kCastRows);
+  auto part = at::empty({ctas, cols}, x.options());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  cast_colsum_kernel<<<ctas, 256, 0, stream>>>(reinterpret_cast<const float4*>(x.data_ptr()),
+                                               reinterpret_cast<uint2*>(out.data_ptr()),
+                                               reinterpret_cast<float4*>(part.data_ptr()), rows, cols / 4);
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part.data_ptr<float>(), sums.data_ptr<float>(), ctas, cols,
+                                                         acc ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(2);
+  return {out, sums};
+}
+
+// out (+)= sum over rows of part [splits, cols] (fp32).
+at::Tensor column_sum(const at::Tensor& part, const c10::optional<at::Tensor>& sum_acc) {
+  TORCH_CHECK(part.is_cuda() && part.is_contiguous() && part.dim() == 2 && part.scalar_type() == at::kFloat,
+              "column_sum: contiguous fp32 [splits, cols]");
+  const c10::cuda::CUDAGuard guard(part.device());
+  const int splits = part.size(0), cols = part.size(1);
+  const bool acc = sum_acc.has_value() && sum_acc->defined();
+  if (acc)
+    TORCH_CHECK(sum_acc->is_contiguous() && sum_acc->scalar_type() == at::kFloat && sum_acc->numel() == cols,
+                "column_sum: sum_acc must be contiguous fp32 [cols]");
+  at::Tensor sums = acc ? *sum_acc : at::empty({cols}, part.options());
+  if (cols == 0) return sums;
+  column_sum_kernel<<<cdiv(cols, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      part.data_ptr<float>(), sums.data_ptr<float>(), splits, cols, acc ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(1);
+  return sums;
 }
 
 at::Tensor bias_gelu_fwd(const at::Tensor& h, const at::Tensor& bias) {

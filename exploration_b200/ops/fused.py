@@ -132,13 +132,7 @@ class ResidualLink:
 
 def _sink_grad(param):
     """``param.grad`` if gradients of ``param`` are accumulated in place (a registered sink)."""
-    sink = gemm._grad_sinks.get(id(param))
-    if sink is None or sink[0]() is not param:
-        return None, None
-    grad = param.grad
-    if grad is None or grad.dtype != torch.float32 or not grad.is_contiguous():
-        return None, None
-    return grad, sink[1]
+    return gemm._sink_target(param)
 
 
 class _LayerNormNative(torch.autograd.Function):

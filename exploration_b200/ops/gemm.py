@@ -87,6 +87,40 @@ def accumulate_weight_grad(param, g, x):
     return weight_grad(g, x)
 
 
+def _sink_target(param):
+    """(param.grad, done callback) when ``param`` is a sink with an fp32 contiguous gradient."""
+    sink = _grad_sinks.get(id(param)) if param is not None else None
+    if sink is None or sink[0]() is not param:
+        return None, None
+    grad = param.grad
+    if grad is None or grad.dtype != torch.float32 or not grad.is_contiguous():
+        return None, None
+    return grad, sink[1]
+
+
+def cast_colsum(d32, bias):
+    """``(d32 as bf16, column sums of d32)``: the bias gradient is added straight into
+    ``bias.grad`` (returned as ``None``) when the bias is a sink."""
+    ext = _native.native(d32)
+    acc, done = _sink_target(bias)
+    g, sums = ext.cast_colsum(d32, acc)
+    if acc is not None:
+        done(bias)
+        return g, None
+    return g, sums
+
+
+def column_sum(partial, bias):
+    """Column sums of fp32 partials, added into ``bias.grad`` when the bias is a sink."""
+    ext = _native.native(partial)
+    acc, done = _sink_target(bias)
+    sums = ext.column_sum(partial, acc)
+    if acc is not None:
+        done(bias)
+        return None
+    return sums
+
+
 def hand_residual(link, dout):
     """The residual input's gradient: left on the link for the paired LayerNorm, or returned."""
     if link is None:
@@ -140,6 +174,7 @@ class LinearResidual(torch.autograd.Function):
         gemm(x2, False, w, False, out, BIAS_RESIDUAL, bias=bias, residual=res)
         ctx.save_for_backward(x2, w)
         ctx.param = weight
+        ctx.bias = bias
         ctx.has_bias = bias is not None
         ctx.shape = x.shape
         ctx.link = link if link is not None and link.armed else None
@@ -150,10 +185,12 @@ class LinearResidual(torch.autograd.Function):
     def backward(ctx, dout):
         x2, w = ctx.saved_tensors
         d32 = _flat(dout)
-        g = d32.to(torch.bfloat16)
+        if ctx.has_bias:
+            g, db = cast_colsum(d32, ctx.bias)
+        else:
+            g, db = d32.to(torch.bfloat16), None
         dx = g @ w
         dw = accumulate_weight_grad(ctx.param, g, x2)
-        db = d32.sum(0) if ctx.has_bias else None
         return dx.view(ctx.shape), dw, db, hand_residual(ctx.link, dout), None
 
 
@@ -173,6 +210,7 @@ class FFNResidual(torch.autograd.Function):
         gemm(u, False, w2b, False, out, BIAS_RESIDUAL, bias=b2, residual=y2)
         ctx.save_for_backward(h2, dgelu, u, w1b, w2b)
         ctx.params = (w1, w2)
+        ctx.biases = (b1, b2)
         ctx.shape = h.shape
         ctx.link = link if link is not None and link.armed else None
         return out.view(y.shape)
@@ -182,13 +220,12 @@ class FFNResidual(torch.autograd.Function):
     def backward(ctx, dout):
         h2, dgelu, u, w1b, w2b = ctx.saved_tensors
         d32 = _flat(dout)
-        g = d32.to(torch.bfloat16)
-        db2 = d32.sum(0)
+        g, db2 = cast_colsum(d32, ctx.biases[1])
         dw2 = accumulate_weight_grad(ctx.params[1], g, u)
         dh_pre = torch.empty_like(dgelu)
         partial = torch.empty(-(-g.shape[0] // TILE_M), dgelu.shape[1], device=g.device, dtype=torch.float32)
         gemm(g, False, w2b, True, dh_pre, GELU_BACK, aux=dgelu, partial=partial)
-        db1 = partial.sum(0)
+        db1 = column_sum(partial, ctx.biases[0])
         dw1 = accumulate_weight_grad(ctx.params[0], dh_pre, h2)
         dh = dh_pre @ w1b
         return dh.view(ctx.shape), hand_residual(ctx.link, dout), dw1, db1, dw2, db2, None

@@ -64,6 +64,7 @@ class FlatParameters:
         fp32_read = {id(m.weight) for m in model.modules() if isinstance(m, torch.nn.Embedding)}
         norm_ids = {id(t) for m in model.modules() if isinstance(m, torch.nn.LayerNorm)
                     for t in (m.weight, m.bias) if t is not None}
+        norm_ids |= {id(m.bias) for m in model.modules() if isinstance(m, torch.nn.Linear) and m.bias is not None}
         small = [p for p in params if p.dim() < 2 or id(p) in fp32_read]
         big = [p for p in params if not (p.dim() < 2 or id(p) in fp32_read)]
         self.params = small + big
@@ -110,7 +111,8 @@ class FlatParameters:
 
     def sink_params(self):
         """Parameters whose gradients the native ops add straight into ``param.grad``: the
-        GEMM weights (sharded region) and the LayerNorm weights and biases."""
+        GEMM weights (sharded region), the LayerNorm weights and biases and the linear
+        layers' biases."""
         return [p for p, off in zip(self.params, self.offsets)
                 if (off >= self.split and p.dim() == 2) or id(p) in self.norm_ids]
 
