@@ -10,20 +10,25 @@ Here the exchange lives inside the GEMMs:
   head-layout slot of the symmetric heap (peer stores), then one peer
   barrier publishes the slots. Used for the query projection (one part)
   and the raw K/V projection (two parts).
-* ``heads_to_linear_residual``: the output projection reads its A operand
-  tile by tile with TMA from the owners' head-layout slots (plain tiled loads
-  of peer memory) and adds bias and the fp32 residual in its epilogue.
+* ``heads_to_linear_residual``: the output projection (bias and fp32
+  residual in its epilogue) over the sequence layout of the owners'
+  head-layout slots. By default each remote row is pulled over NVLink once
+  (``gather_rows``, 16-byte peer loads) and the tcgen05 GEMM reads the
+  landed copy; ``EB200_ULYSSES_GATHER=fused`` reads the A tiles with TMA
+  straight from peer memory inside the GEMM instead (see ``gather_mode``).
 
-Backward is the mirror image: the gradient of a scatter is a gather-GEMM
-(``dx = dY W``) and the gradient of a gather is a scatter-GEMM
+Backward is the mirror image: the gradient of a scatter is a gather and a
+GEMM (``dx = dY W``) and the gradient of a gather is a scatter-GEMM
 (``dctx = dOut W`` stored to the head owners). Weight gradients use the
-gathered activation as a plain local operand (``gather_rows``).
+landed sequence-layout activation as a plain local operand.
 
 Every rank issues the same sequence of heap allocations and barriers (the
 model runs the same layers on every rank), which keeps slot offsets
 identical and the barrier epochs aligned.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -36,6 +41,20 @@ TILE_M = 128
 
 def _bf16(param):
     return _cached_copy(param, torch.bfloat16)
+
+
+def gather_mode() -> str:
+    """How the head -> sequence direction reads the owners' buffers.
+
+    ``landed`` (default): ``gather_rows`` pulls every remote row over NVLink
+    once into a local sequence-layout buffer (16-byte peer loads) and the
+    tcgen05 GEMM reads it from there; the landed copy is kept for the weight
+    gradient. ``fused`` (``EB200_ULYSSES_GATHER=fused``): the GEMM's TMA
+    producer reads A tiles straight from the owners' buffers, which overlaps
+    transfer and math inside one kernel but fetches each remote row once per
+    output-column tile (N / 256 times).
+    """
+    return "fused" if os.environ.get("EB200_ULYSSES_GATHER", "landed") == "fused" else "landed"
 
 
 class _ProjectToHeads(torch.autograd.Function):
@@ -68,10 +87,13 @@ class _ProjectToHeads(torch.autograd.Function):
         heap.barrier()
         ptrs = heap.peer_ptrs(gslot)
         dx = torch.empty(batch * n_local, x2.shape[1], device=x2.device, dtype=torch.bfloat16)
-        # dx = dY_seq W  (W stored [parts*dim, K] = [K_red, N]: MN-major B)
-        U.ext.gemm_gather(ptrs, U.rank, parts, batch, n_local, C, w, True, dx, G.STORE_BF16, None, None)
         dy_seq = torch.empty(batch * n_local, parts * U.world * C, device=x2.device, dtype=torch.bfloat16)
         U.ext.gather_rows(ptrs, U.rank, parts, batch, n_local, C, dy_seq)
+        # dx = dY_seq W  (W stored [parts*dim, K] = [K_red, N]: MN-major B)
+        if gather_mode() == "fused":
+            U.ext.gemm_gather(ptrs, U.rank, parts, batch, n_local, C, w, True, dx, G.STORE_BF16, None, None)
+        else:
+            G.gemm(dy_seq, False, w, True, dx, G.STORE_BF16)
         dw = G.accumulate_weight_grad(ctx.param, dy_seq, x2)
         return dx.view(shape), dw, None, None, None, None
 
@@ -90,8 +112,16 @@ class _HeadsToLinearResidual(torch.autograd.Function):
         if not res.is_contiguous():
             res = res.contiguous()
         out = torch.empty(res.shape, device=res.device, dtype=torch.float32)
-        U.ext.gemm_gather(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, w, False, out,
-                          G.BIAS_RESIDUAL, bias, res)
+        ctx_seq = None
+        if gather_mode() == "fused":
+            U.ext.gemm_gather(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, w, False, out,
+                              G.BIAS_RESIDUAL, bias, res)
+        else:
+            # Each remote row crosses NVLink once; the landed copy also serves dW.
+            ctx_seq = torch.empty(batch * n_local, U.world * C, device=res.device, dtype=torch.bfloat16)
+            U.ext.gather_rows(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, ctx_seq)
+            G.gemm(ctx_seq, False, w, False, out, G.BIAS_RESIDUAL, bias=bias, residual=res)
+        ctx.ctx_seq = ctx_seq
         ctx.save_for_backward(w)
         ctx.param = weight
         ctx.link = link if link is not None and link.armed else None
@@ -112,8 +142,10 @@ class _HeadsToLinearResidual(torch.autograd.Function):
         U.ext.gemm_scatter(g, w, True, heap.peer_ptrs(gslot), U.rank, 1, batch, n_local, C)
         heap.barrier()
         dheads = heap.tensor(gslot, (batch, n_local * U.world, hpr, hd))
-        ctx_seq = torch.empty(batch * n_local, U.world * C, device=g.device, dtype=torch.bfloat16)
-        U.ext.gather_rows(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, ctx_seq)
+        ctx_seq, ctx.ctx_seq = ctx.ctx_seq, None
+        if ctx_seq is None:
+            ctx_seq = torch.empty(batch * n_local, U.world * C, device=g.device, dtype=torch.bfloat16)
+            U.ext.gather_rows(heap.peer_ptrs(slot), U.rank, 1, batch, n_local, C, ctx_seq)
         dw = G.accumulate_weight_grad(ctx.param, g, ctx_seq)
         db = d32.sum(0) if has_bias else None
         return dheads, dw, db, G.hand_residual(ctx.link, dout), None, None

@@ -13,6 +13,9 @@ the Stack G-round projections around the gated attention:
 * ``out_gather``: the output projection with the residual epilogue whose A
   operand is read tile by tile from the owners' head buffers (``gemm_gather``)
   after the barrier that makes them ready: head layout in, sequence layout out.
+* ``out_landed``: the same direction as two kernels, the default in
+  training: ``gather_rows`` pulls each remote row over NVLink once into a
+  local buffer, then the tcgen05 GEMM with the residual epilogue reads it.
 * ``*_nccl``: the baseline of each: the same GEMM (cuBLAS) plus
   ``all_to_all_single`` and the layout permutes (the reference's path,
   st/runtime/parallel.py:16-27).
@@ -117,6 +120,13 @@ def main(argv=None):
         ext.gemm_gather(heap.peer_ptrs(heads_slot), rank, 1, 1, n_local, C, w_o, False, out,
                         G.BIAS_RESIDUAL, None, residual)
 
+    landed = torch.empty(n_local, dim, device=device, dtype=torch.bfloat16)
+
+    def out_landed():
+        heap.barrier()
+        ext.gather_rows(heap.peer_ptrs(heads_slot), rank, 1, 1, n_local, C, landed)
+        G.gemm(landed, False, w_o, False, out, G.BIAS_RESIDUAL, residual=residual)
+
     def q_nccl():
         y = torch.mm(x, w_q.t()).view(1, n_local, heads, hd)
         return exchange(y, dist.group.WORLD, True)
@@ -135,7 +145,8 @@ def main(argv=None):
         return torch.mm(x, w_q.t())
 
     ops = {"q_scatter": q_scatter, "q_nccl": q_nccl, "kv_scatter": kv_scatter, "kv_nccl": kv_nccl,
-           "out_gather": out_gather, "out_nccl": out_nccl, "q_gemm_local": gemm_q_local}
+           "out_gather": out_gather, "out_landed": out_landed, "out_nccl": out_nccl,
+           "q_gemm_local": gemm_q_local}
     times = {name: _time(fn, args.warmup, args.iterations) for name, fn in ops.items()}
     t = torch.tensor([times[k] for k in ops], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -148,7 +159,8 @@ def main(argv=None):
 
     proj = {"q_scatter": (2 * n_local * dim * dim, n_local * dim * 2 * remote),
             "kv_scatter": (2 * n_local * dim * 2 * dim, n_local * 2 * dim * 2 * remote),
-            "out_gather": (2 * n_local * dim * dim, n_local * dim * 2 * remote)}
+            "out_gather": (2 * n_local * dim * dim, n_local * dim * 2 * remote),
+            "out_landed": (2 * n_local * dim * dim, n_local * dim * 2 * remote)}
     report = {"config": Path(args.config).stem, "length": args.length, "world": world, "n_local": n_local,
               "dim": dim, "heads": heads, "peak_tflops": peak / 1e12, "peer_gbs": PEER_BYTES_PER_S / 1e9,
               "us_max_over_ranks": {k: round(v, 1) for k, v in times.items()}}

@@ -49,9 +49,11 @@ def _need_two():
         pytest.skip("needs two or more GPUs")
 
 
-@pytest.mark.parametrize("world", _worlds())
-def test_fused_ulysses_matches_nccl(world):
-    results = _launch("parity", world)
+@pytest.mark.parametrize("world,gather", [(w, "landed") for w in _worlds()] + [(2, "fused")])
+def test_fused_ulysses_matches_nccl(world, gather):
+    """``gather``: the head -> sequence direction lands remote rows once (default) or
+    reads them inside the GEMM (``EB200_ULYSSES_GATHER=fused``)."""
+    results = _launch("parity", world, {"EB200_ULYSSES_GATHER": gather})
     for r in results:
         assert r["device_errors"] == [0, 0]
         assert abs(r["fused_loss"] - r["nccl_loss"]) <= 2e-2 * max(1.0, abs(r["nccl_loss"]))
