@@ -142,7 +142,8 @@ def run_ours(args, rank, world, local_rank):
                                 loss_chunk=targs.loss_chunk)
     model = build_model({"model": "stack", **options}, execution=execution, device=device)
     model.train()
-    fused_exchange = parallel.attach_fused(device)
+    fused_exchange = parallel.attach_fused(
+        device, max(512 << 20, parallel.fused_heap_bytes(model, 1, args.length)))
     graphed = args.cuda_graph
     if graphed:
         from exploration_b200.runtime.engine import lr_factor

@@ -596,9 +596,10 @@ struct alignas(1024) LtDkvSmem {
 };
 
 constexpr uint32_t kDkvTmemCols = 512;
+constexpr int kDkvThreads = 384;          // control warps 0-3 + two compute warpgroups
 constexpr uint32_t kColDp = 160, kColDs = 160, kColDv = 320, kColDk = 384;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDkvThreads, 1)
 local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
                     const __grid_constant__ CUtensorMap t_prev, const __grid_constant__ CUtensorMap t_dout,
                     const __grid_constant__ CUtensorMap t_dout16, LtBwdArgs a, int owner_ctas) {
@@ -615,11 +616,11 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
     mbar_init(&sm.v_full, 1);
     mbar_init(&sm.q_full, 1);
     mbar_init(&sm.g_full, 1);
-    mbar_init(&sm.rot_done, 128);
+    mbar_init(&sm.rot_done, 256);
     mbar_init(&sm.s_full, 1);
     mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.p_full, 128);
-    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.p_full, 256);
+    mbar_init(&sm.ds_full, 256);
     mbar_init(&sm.dv_full, 1);
     mbar_init(&sm.dk_full, 1);
     sm.abort = 0;
@@ -627,7 +628,7 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
   }
   if (warp == 2) tmem_alloc(&sm.tmem_base, kDkvTmemCols);
   // Per-query statistics of rows s0 .. s0 + 143 (base-2 lse, delta).
-  for (int i = threadIdx.x; i < kKeys; i += kThreads) {
+  for (int i = threadIdx.x; i < kKeys; i += kDkvThreads) {
     const int t = s0 + i;
     float l2 = 0.f, d = 0.f;
     if (t >= 0 && t < a.n) {
@@ -717,51 +718,112 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
       }
     }
   } else if (warp >= 4) {
-    const int tid = threadIdx.x - 128;
-    const int w = warp - 4;
+    // Two compute warpgroups share every key row (TMEM lane): group 0 (warps
+    // 4-7) owns band columns j in [0, 32) and dV, group 1 (warps 8-11) owns
+    // j in [32, 48), the zero columns outside the band and dK. P^T and dS^T
+    // overwrite the fp32 columns they are computed from, so both groups load
+    // their values before either stores (named barrier over the 256 threads).
+    const int grp = (warp - 4) >> 2;
+    const int w = warp & 3;                        // TMEM lane quarter: rows 32 w ..
+    const int tid = threadIdx.x - 128 - grp * 128;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
     // Origin 16 rows before s0: key row k at offset k + 16, query row i at i + 16.
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
-    if (ok) rotate_tile<kM>(sm.k, kB, a.cos, a.sin, tid);
-    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
-    if (ok) rotate_tile<kKeys>(sm.q, kB, a.cos, a.sin, tid);
+    // Group 0 rotates K while group 1 rotates Q.
+    bool ok;
+    if (grp == 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+      if (ok) rotate_tile<kM>(sm.k, kB, a.cos, a.sin, tid);
+    } else {
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
+      if (ok) rotate_tile<kKeys>(sm.q, kB, a.cos, a.sin, tid);
+    }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive(&sm.rot_done);
     const int kr = tid, tk = s0 + kr;              // key row and token
     const bool key_live = bwd_key_ok(a, tk) && (!halo_cta || kr >= kM - kB);
     const int off = lane >= 16 ? kB : 0;           // query window start relative to column 32 w
-    float p[48];
+    const int j0 = grp == 0 ? 0 : 32, nj = grp == 0 ? 32 : 16;
+    uint32_t zero[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) zero[c] = 0u;
+    // Stores this group's 16-column chunks of band values v (bf16 pairs) at `addr`.
+    auto store_mine = [&](uint32_t addr, const float (&v)[32]) {
+#pragma unroll
+      for (int rel = 0; rel < 2; ++rel) {
+        if (rel * 16 < nj) {
+          uint32_t packed[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) packed[c] = pack_bf16(v[rel * 16 + 2 * c], v[rel * 16 + 2 * c + 1]);
+          tmem_st8(addr + (2 * w + j0 / 16 + rel) * 8, packed);
+        }
+      }
+      if (grp == 1) {
+#pragma unroll
+        for (int chunk = 0; chunk < kKeys / 16; ++chunk)
+          if (chunk < 2 * w || chunk > 2 * w + 2) tmem_st8(addr + chunk * 8, zero);
+      }
+    };
+    auto load_mine = [&](uint32_t addr, float (&v)[32]) {
+      uint32_t r[32];
+      if (grp == 0) {
+        tmem_ld32(addr + 32 * w, r);
+      } else {
+        uint32_t r16[16];
+        tmem_ld16(addr + 32 * w + 32, r16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          r[i] = r16[i];
+          r[i + 16] = 0u;
+        }
+      }
+      tc_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    };
+    float p[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) p[i] = 0.f;
     ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.s_full, 0, abort, a.err, kSiteSFull));
     if (ok) {
       tc_fence_after();
-      float x[48];
-      load_band48(lane_addr + 32 * w, x);
+      float x[32];
+      load_mine(0, x);
       const float scale = 0.125f * kLog2e;
 #pragma unroll
-      for (int j = 0; j < 48; ++j) {
+      for (int i = 0; i < 32; ++i) {
+        const int j = j0 + i;
         const int qi = 32 * w + j, tq = s0 + qi;   // query index in [0, 144) and token
-        const bool in = key_live && j >= off && j < off + 2 * kB && qi >= kr && tq >= 0 && tq < a.n;
-        p[j] = in ? ex2(fmaf(x[j], scale, -sm.lse2[qi])) : 0.f;
+        const bool in = i < nj && key_live && j >= off && j < off + 2 * kB && qi >= kr && tq >= 0 && tq < a.n;
+        p[i] = in ? ex2(fmaf(x[i], scale, -sm.lse2[qi < kKeys ? qi : kKeys - 1])) : 0.f;
       }
-      store_band_bf16(lane_addr, w, p);            // P^T over S^T's columns
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (ok) {
+      store_mine(lane_addr, p);                    // P^T over S^T's columns
       tc_wait_st();
     }
     tc_fence_before();
     mbar_arrive(&sm.p_full);
     ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, 0, abort, a.err, kSiteSFull));
+    float dp[32];
     if (ok) {
       tc_fence_after();
-      float dp[48];
-      load_band48(lane_addr + kColDp + 32 * w, dp);
+      load_mine(kColDp, dp);
 #pragma unroll
-      for (int j = 0; j < 48; ++j) dp[j] = p[j] * (dp[j] - sm.delta[32 * w + j]);
-      store_band_bf16(lane_addr + kColDs, w, dp);  // dS^T over dP^T's columns
+      for (int i = 0; i < 32; ++i) {
+        const int qi = 32 * w + j0 + i;
+        dp[i] = i < nj ? p[i] * (dp[i] - sm.delta[qi < kKeys ? qi : kKeys - 1]) : 0.f;
+      }
+    }
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    if (ok) {
+      store_mine(lane_addr + kColDs, dp);          // dS^T over dP^T's columns
       tc_wait_st();
     }
     tc_fence_before();
     mbar_arrive(&sm.ds_full);
-    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dv_full, 0, abort, a.err, kSiteODone) &&
-                                           mbar_wait(&sm.dk_full, 0, abort, a.err, kSiteODone));
+    ok = ok && __all_sync(0xffffffffu, grp == 0 ? mbar_wait(&sm.dv_full, 0, abort, a.err, kSiteODone)
+                                                : mbar_wait(&sm.dk_full, 0, abort, a.err, kSiteODone));
     if (ok) {
       tc_fence_after();
       float y[64];
@@ -771,13 +833,16 @@ local_tc_dkv_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
       } else if (tk < a.n) {
         base = a.dqkv + ((static_cast<int64_t>(batch) * a.n + tk) * 3 * H + head) * kD;
       }
-      load_tmem64(lane_addr + kColDv, y);
-      if (base) store_row64(base + 2 * H * kD, y);
-      load_tmem64(lane_addr + kColDk, y);
+      if (grp == 0) {
+        load_tmem64(lane_addr + kColDv, y);
+        if (base) store_row64(base + 2 * H * kD, y);
+      } else {
+        load_tmem64(lane_addr + kColDk, y);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) y[i] *= 0.125f;
-      unrotate_row(y, kr + kB, a.cos, a.sin);
-      if (base) store_row64(base + H * kD, y);
+        for (int i = 0; i < 64; ++i) y[i] *= 0.125f;
+        unrotate_row(y, kr + kB, a.cos, a.sin);
+        if (base) store_row64(base + H * kD, y);
+      }
     }
   }
   if (warp == 0 && lane == 0 && *abort) {
@@ -923,7 +988,7 @@ std::vector<at::Tensor> local_tc_bwd(const at::Tensor& dout, const at::Tensor& q
     auto kernel = local_tc_dkv_kernel;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     trace("dkv attribute");
-    kernel<<<dim3(ctas + (has_prev ? 1 : 0), heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout,
+    kernel<<<dim3(ctas + (has_prev ? 1 : 0), heads, batch), kDkvThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout,
                                                                                        t_dout16, args, ctas);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     trace("dkv kernel");

@@ -156,10 +156,26 @@ class ParallelContext:
         return cls(world, rank, cp_size, rank % cp_size, world // cp_size, rank // cp_size,
                    cp_group, dp_group)
 
+    def fused_heap_bytes(self, model, batch: int, length: int) -> int:
+        """Symmetric-heap bytes one micro-step of ``model`` needs for the fused exchange.
+
+        Per step the heap holds head-layout slots of ``batch x length x C``
+        bf16 values (C = heads per rank x head dim): K and V (two) plus their
+        gradients (two), and per read round the query, the attention output and
+        their gradients (four); 16 MB covers alignment and signal words.
+        """
+        heads, hd = int(model.heads), int(model.hd)
+        C = heads // max(1, self.cp_size) * hd
+        rounds = max(1, len(getattr(model, "reads", [])) or 1)
+        slot = batch * length * C * 2
+        return (4 + 4 * rounds) * slot + (16 << 20)
+
     def attach_fused(self, device, nbytes: int = 0) -> bool:
         """Attach the NVLink-fused Ulysses exchange (CUDA, CP > 1; collective).
 
-        Disabled with ``EB200_FUSED_ULYSSES=0`` (the NCCL path is then used).
+        ``nbytes``: heap size per rank (``fused_heap_bytes``; default 512 MB or
+        ``EB200_HEAP_BYTES``). Disabled with ``EB200_FUSED_ULYSSES=0`` (the NCCL
+        path is then used).
         """
         if self.cp_size == 1 or self.ulysses is not None:
             return self.ulysses is not None

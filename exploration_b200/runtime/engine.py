@@ -424,7 +424,9 @@ def run(args):
             dataset = None
         model.to(device)
         if device.type == "cuda" and isinstance(model, StackModel) and args.backend != "torch":
-            parallel.attach_fused(device)
+            length = max(args.length, getattr(args, "eval_length", 0) or 0)
+            parallel.attach_fused(device, max(512 << 20, parallel.fused_heap_bytes(
+                model, args.batch_size, length)))
         if args.command == "train":
             return train(args, model, parallel, ck, dataset, validation)
         return evaluate(args, model, parallel, dataset)
