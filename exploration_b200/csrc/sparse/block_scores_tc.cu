@@ -57,8 +57,10 @@ struct alignas(1024) ScoreSmem {
   int pos[N];
 };
 
+// Up to 16 queries the kernel fits 80 registers, so two CTAs share an SM (the
+// host sizes the grid for two per SM).
 template <int D, int N, int B>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, N <= 16 ? 2 : 1)
 block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, ScoreArgs a) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
   using Smem = ScoreSmem<D, N>;
@@ -168,28 +170,45 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
       tc_wait_ld();
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[buf]);                        // the values are in registers
+      // Eight query columns at a time, each reduction step issued for all
+      // eight before the next, so the shuffle latencies overlap.
 #pragma unroll
-      for (int j = 0; j < kHalf; ++j) {
-        const int c = grp * kHalf + j;
-        const float x = key < a.keys ? __uint_as_float(r[j]) * scale2 : kNegInf;
-        float m = x;
+      for (int j0 = 0; j0 < kHalf; j0 += 8) {
+        float x[8], m[8], e[8];
 #pragma unroll
-        for (int o = 1; o < B; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float e = m == kNegInf ? 0.f : ex2(x - m);
+        for (int j = 0; j < 8; ++j) {
+          x[j] = key < a.keys ? __uint_as_float(r[j0 + j]) * scale2 : kNegInf;
+          m[j] = x[j];
+        }
 #pragma unroll
-        for (int o = 1; o < B; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
-        const int p = sm.pos[c];
-        const bool visible = full && p >= 0 && gid < p / B - 1 && c < a.queries && m != kNegInf;
-        if (owner && c < a.queries && g < a.groups) {
-          const float sb2 = visible ? m + lg2(e) : kNegInf;
-          a.scores[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.groups + g] =
-              visible ? sb2 * 0.6931471805599453f : kNegInf;
-          if (visible) {
-            if (sb2 > zm[j]) {
-              zs[j] = zs[j] * ex2(zm[j] - sb2) + 1.f;
-              zm[j] = sb2;
-            } else {
-              zs[j] += ex2(sb2 - zm[j]);
+        for (int o = 1; o < B; o <<= 1) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = m[j] == kNegInf ? 0.f : ex2(x[j] - m[j]);
+#pragma unroll
+        for (int o = 1; o < B; o <<= 1) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) e[j] += __shfl_xor_sync(0xffffffffu, e[j], o);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int jj = j0 + j;
+          const int c = grp * kHalf + jj;
+          const int p = sm.pos[c];
+          const bool visible = full && p >= 0 && gid < p / B - 1 && c < a.queries && m[j] != kNegInf;
+          if (owner && c < a.queries && g < a.groups) {
+            const float sb2 = visible ? m[j] + lg2(e[j]) : kNegInf;
+            a.scores[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.groups + g] =
+                visible ? sb2 * 0.6931471805599453f : kNegInf;
+            if (visible) {
+              if (sb2 > zm[jj]) {
+                zs[jj] = zs[jj] * ex2(zm[jj] - sb2) + 1.f;
+                zm[jj] = sb2;
+              } else {
+                zs[jj] += ex2(sb2 - zm[jj]);
+              }
             }
           }
         }
