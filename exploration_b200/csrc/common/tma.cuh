@@ -93,6 +93,27 @@ inline CUtensorMap make_plane_map(const void* base, int64_t planes, int64_t rows
   return map;
 }
 
+// bf16 tensor [planes, rows, cols] (cols contiguous, dense) for TMA stores of
+// unswizzled boxes of box_cols x box_rows x 1 (rows packed in shared memory).
+// `base` may be a peer GPU's memory mapped into this process.
+inline CUtensorMap make_store_plane_map(const void* base, int64_t planes, int64_t rows, int64_t cols, int box_cols,
+                                        int box_rows) {
+  bind_primary_context();
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((cols * 2) % 16 == 0 && (box_cols * 2) % 16 == 0, "TMA rows must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2, static_cast<cuuint64_t>(rows) * cols * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult res = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", static_cast<int>(res));
+  return map;
+}
+
 // One error slot per device, allocated on first use and kept for the process
 // (defined in attention/gated_entry.cu).
 sm100::ErrorSlot* device_error_slot(int device);

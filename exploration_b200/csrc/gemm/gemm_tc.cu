@@ -23,6 +23,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "../common/sm100.cuh"
 #include "../common/tma.cuh"
 
@@ -56,11 +59,12 @@ constexpr int kMaxPeers = 8;
 // In the sequence layout a row has parts * dim columns, dim = world * C.
 struct PeerLayout {
   int world, rank, parts, batch, n_local, n_total, C, dim;
+  int tma_store;                   // scatter through TMA stores of 32 x 32 blocks (PeerMaps hold the targets)
   __nv_bfloat16* dst[kMaxPeers];   // scatter targets (possibly peer memory)
 };
 
 struct PeerMaps {
-  CUtensorMap map[kMaxPeers];      // gather sources, one 3-D map per rank
+  CUtensorMap map[kMaxPeers];      // gather sources or scatter targets, one 3-D map per rank
 };
 
 struct GemmArgs {
@@ -86,7 +90,8 @@ struct alignas(1024) GemmSmem {
   uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
-  float4 stage[8][32 * 4]; // per epilogue warp: 32 rows x 16 fp32 columns, 16-byte units swizzled
+  alignas(128) float4 stage[8][32 * 4]; // per epilogue warp: 32 rows x 16 fp32 columns, 16-byte units swizzled
+                                         // (peer-scatter epilogue: a 32 x 32 bf16 block for one TMA store)
   float colsum[8][BN / 2]; // per epilogue warp column partials of the GELU-backward epilogue
 };
 
@@ -357,6 +362,39 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       for (int c0 = grp * (BN / 2); c0 < (grp + 1) * (BN / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + acc * BN + c0, r);
+        if constexpr (EPI == kScatterBf16) {
+          if (g.peer.tma_store) {
+            // The warp's 32 rows x these 32 columns go to one owner as one TMA
+            // store: each lane packs its row (64 bytes) into the staging block.
+            tc_wait_ld();
+            const int n = tn * BN + c0;
+            if (n >= g.N) continue;
+            __nv_bfloat16* block = reinterpret_cast<__nv_bfloat16*>(stage);
+            if (lane == 0) bulk_wait_read_all();             // the previous store has read the block
+            __syncwarp();
+            uint4* row = reinterpret_cast<uint4*>(block + lane * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t* v = r + 8 * q;
+              row[q] = make_uint4(pack_bf16(__uint_as_float(v[0]) * g.alpha, __uint_as_float(v[1]) * g.alpha),
+                                  pack_bf16(__uint_as_float(v[2]) * g.alpha, __uint_as_float(v[3]) * g.alpha),
+                                  pack_bf16(__uint_as_float(v[4]) * g.alpha, __uint_as_float(v[5]) * g.alpha),
+                                  pack_bf16(__uint_as_float(v[6]) * g.alpha, __uint_as_float(v[7]) * g.alpha));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const PeerLayout& L = g.peer;
+              const int m0 = tm * kBM + wr * 32;
+              const int b = m0 / L.n_local, t0 = m0 - b * L.n_local;
+              const int part = n / L.dim, within = n - part * L.dim;
+              const int owner = within / L.C, c = within - owner * L.C;
+              tma_store_3d(&pm.map[owner], block, c, L.rank * L.n_local + t0, part * L.batch + b);
+              bulk_commit();
+            }
+            continue;
+          }
+        }
         // GELU backward: the kept gelu' of this chunk's 8 (row, 4-column) groups is
         // loaded while the TMEM load is in flight.
         uint2 aux_raw[2][4];
@@ -428,7 +466,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     }
     // Peer stores complete at system scope before the kernel ends, so a
     // barrier issued after it publishes them.
-    if constexpr (EPI == kScatterBf16) __threadfence_system();
+    if constexpr (EPI == kScatterBf16) {
+      if (g.peer.tma_store && lane == 0) bulk_wait_all();   // this warp's stores are complete
+      __threadfence_system();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -454,12 +495,13 @@ void launch_gemm(const CUtensorMap& ta, const PeerMaps& pm, const at::Tensor& b,
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-void run_gemm(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args, cudaStream_t stream) {
+void run_gemm(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args, cudaStream_t stream,
+              const PeerMaps* pm = nullptr) {
   // TMA maps: inner (contiguous) dimension first.
   CUtensorMap ta = A_MN ? make_matrix_map(a.data_ptr(), K, M, a.stride(0), kBK)     // [K, M], box 64m x 64k
                         : make_matrix_map(a.data_ptr(), M, K, a.stride(0), kBM);    // [M, K], box 64k x 128m
   PeerMaps none{};
-  launch_gemm<BN, A_MN, B_MN, EPI, false>(ta, none, b, M, N, K, args, stream);
+  launch_gemm<BN, A_MN, B_MN, EPI, false>(ta, pm ? *pm : none, b, M, N, K, args, stream);
 }
 
 bool wide_tiles(int M, int N) {
@@ -609,14 +651,22 @@ void gemm_scatter(const at::Tensor& a, const at::Tensor& b, bool b_mn, const std
   const c10::cuda::CUDAGuard guard(a.device());
   GemmArgs args = base_args(M, N, K, a);
   args.vec = (C % 4) == 0;
+  // 32 x 32 blocks stay inside one owner's columns and one batch's rows.
+  static const bool tma_off = std::getenv("EB200_SCATTER_TMA") != nullptr &&
+                              std::string(std::getenv("EB200_SCATTER_TMA")) == "0";
+  L.tma_store = !tma_off && C % 32 == 0 && n_local % 32 == 0 ? 1 : 0;
   args.peer = L;
+  PeerMaps pm{};
+  if (L.tma_store)
+    for (int r = 0; r < world; ++r)
+      pm.map[r] = make_store_plane_map(reinterpret_cast<const void*>(dst[r]), parts * batch, L.n_total, C, 32, 32);
   auto stream = at::cuda::getCurrentCUDAStream();
   if (b_mn) {
-    if (wide_tiles(M, N)) run_gemm<256, false, true, kScatterBf16>(a, b, M, N, K, args, stream);
-    else run_gemm<128, false, true, kScatterBf16>(a, b, M, N, K, args, stream);
+    if (wide_tiles(M, N)) run_gemm<256, false, true, kScatterBf16>(a, b, M, N, K, args, stream, &pm);
+    else run_gemm<128, false, true, kScatterBf16>(a, b, M, N, K, args, stream, &pm);
   } else {
-    if (wide_tiles(M, N)) run_gemm<256, false, false, kScatterBf16>(a, b, M, N, K, args, stream);
-    else run_gemm<128, false, false, kScatterBf16>(a, b, M, N, K, args, stream);
+    if (wide_tiles(M, N)) run_gemm<256, false, false, kScatterBf16>(a, b, M, N, K, args, stream, &pm);
+    else run_gemm<128, false, false, kScatterBf16>(a, b, M, N, K, args, stream, &pm);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(1);
