@@ -36,7 +36,7 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-BASELINE_TOKENS_PER_S = None          # BASELINE.md publishes no B200 number for this config
+BASELINE_TOKENS_PER_S = None          # the reference publishes no B200 number for this config
 METRIC = "train_tokens_per_second"
 CONFIG = ROOT / "configs" / "stack_100m.json"
 
