@@ -61,19 +61,32 @@ def parse():
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """``nvidia-smi`` clock and throttle-reason samples every 50 ms, kept for the timed window.
+
+    The sampler starts before the warm-up steps (the process needs a moment to
+    produce its first line) and ``mark(start, end)`` sets the timed window in
+    wall-clock time; ``summary()`` reports the samples inside the window, or,
+    when the window is shorter than the sampling interval, the nearest sample
+    on each side of it (``"window": "adjacent"``).
+    """
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, indices):
+    def __init__(self, indices, interval_ms: int = 50):
         self.indices = set(indices)
+        self.interval_ms = interval_ms
         self.proc = None
         self.lines = []
+        self.window = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", str(self.interval_ms)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -84,33 +97,62 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def __exit__(self, *exc):
+    def mark(self, start: float, end: float) -> None:
+        """The timed window, as ``time.time()`` values."""
+        self.window = (start, end)
+
+    def stop(self):
         if self.proc is not None:
+            time.sleep(2 * self.interval_ms / 1e3)        # one more sample after the window
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.proc = None
 
-    def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.indices:
-                continue
+    @staticmethod
+    def _when(stamp: str):
+        from datetime import datetime
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                return datetime.strptime(stamp, fmt).timestamp()
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        return None
+
+    def samples(self):
+        out = []
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10 or not parts[1].isdigit() or int(parts[1]) not in self.indices:
+                continue
+            try:
+                sm, mx = float(parts[2]), float(parts[3])
+            except ValueError:
+                continue
+            reasons = {name for name, flag in zip(self.REASONS, parts[6:10]) if flag.lower() == "active"}
+            out.append((self._when(parts[0]), sm, mx, reasons))
+        return out
+
+    def summary(self):
+        samples = self.samples()
+        chosen, window = samples, "unbounded"
+        if self.window is not None and samples and all(t is not None for t, *_ in samples):
+            t0, t1 = self.window
+            inside = [s for s in samples if t0 <= s[0] <= t1]
+            if inside:
+                chosen, window = inside, "timed"
+            else:
+                before = [s for s in samples if s[0] < t0][-1:]
+                after = [s for s in samples if s[0] > t1][:1]
+                chosen, window = before + after, "adjacent"
+        if not chosen:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set().union(*(r for *_, r in chosen))
+        return {"sm_mhz": statistics.median(s[1] for s in chosen), "sm_max_mhz": max(s[2] for s in chosen),
+                "reasons": sorted(reasons), "samples": len(chosen), "window": window,
+                "interval_ms": self.interval_ms}
 
 
 # ---------------------------------------------------------------------------
@@ -175,6 +217,7 @@ def run_ours(args, rank, world, local_rank):
         d2h = stats.element_size() * stats.numel()
         return loss
 
+    sampler = ClockSampler([local_rank]).start() if rank == 0 else None
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
@@ -183,17 +226,19 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = ext.launch_count()
-    sampler = ClockSampler([local_rank]) if rank == 0 else contextlib.nullcontext()
-    with sampler:
-        wall0 = time.perf_counter()
-        start.record()
-        losses = [step(args.warmup + i) for i in range(args.steps)]
-        end.record()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - wall0
+    window0 = time.time()
+    wall0 = time.perf_counter()
+    start.record()
+    losses = [step(args.warmup + i) for i in range(args.steps)]
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if sampler is not None:
+        sampler.mark(window0, time.time())
+        sampler.stop()
     launches = ext.launch_count() - launches0
     if graphed:
         launches += trainer.graph_launches * args.steps          # kernels replayed from the graph
@@ -217,7 +262,7 @@ def run_ours(args, rank, world, local_rank):
                        "l2": "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)",
                        "ulysses_exchange": "nvlink-fused" if fused_exchange else ("nccl" if cp > 1 else "none"),
                        "cuda_graph": bool(graphed), "optimizer_shard": bool(targs.optimizer_shard)},
-            "clocks": sampler.summary(),
+            "clocks": sampler.summary() if sampler is not None else None,
             "e2e": {"value": round(tokens / wall_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "gpu_launches": int(launches),

@@ -1,0 +1,46 @@
+"""bench.py pieces that run without a GPU: the clock sampler's timed window."""
+import importlib.util
+import time
+from datetime import datetime
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_module", ROOT / "bench.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def _line(t, index, sm, hw="Not Active", power_cap="Not Active"):
+    stamp = datetime.fromtimestamp(t).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+    return f"{stamp}, {index}, {sm}, 1965, 900, 0x0, {hw}, Not Active, Not Active, {power_cap}"
+
+
+def test_clock_sampler_keeps_the_timed_window():
+    sampler = _bench().ClockSampler([0])
+    now = time.time()
+    sampler.lines = [_line(now - 0.1, 0, 1965), _line(now + 0.02, 0, 1800, power_cap="Active"),
+                     _line(now + 0.04, 0, 1850), _line(now + 0.3, 0, 1000, hw="Active"),
+                     _line(now + 0.03, 1, 500, hw="Active")]          # another GPU: ignored
+    sampler.mark(now, now + 0.05)
+    summary = sampler.summary()
+    assert summary["window"] == "timed" and summary["samples"] == 2
+    assert summary["sm_mhz"] == 1825 and summary["reasons"] == ["sw_power_cap"]
+
+
+def test_clock_sampler_short_window_uses_adjacent_samples():
+    sampler = _bench().ClockSampler([0])
+    now = time.time()
+    sampler.lines = [_line(now - 0.04, 0, 1965), _line(now + 0.06, 0, 1900)]
+    sampler.mark(now, now + 0.01)
+    summary = sampler.summary()
+    assert summary["window"] == "adjacent" and summary["samples"] == 2
+
+
+def test_clock_sampler_without_samples():
+    sampler = _bench().ClockSampler([0])
+    sampler.mark(0.0, 1.0)
+    assert sampler.summary()["reasons"] == ["unsampled"]
