@@ -1,6 +1,6 @@
 """Headline benchmark: Stack training throughput (tokens/s) on B200.
 
-Workload (BASELINE.json): configs/stack_100m.json (d=1024, 16 heads, block 16,
+Workload: configs/stack_100m.json (d=1024, 16 heads, block 16,
 ``Lx7,G``), random-token task (next-token loss on every position), sequence
 length 8192, batch 1 per data-parallel replica, bf16 autocast with fp32
 master weights and AdamW, Ulysses context parallelism over all N ranks
@@ -39,13 +39,27 @@ ROOT = Path(__file__).resolve().parent
 BASELINE_TOKENS_PER_S = None          # the reference publishes no B200 number for this config
 METRIC = "train_tokens_per_second"
 CONFIG = ROOT / "configs" / "stack_100m.json"
+L2_NOTE = "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)"
+LOG_WINDOW = 10                       # the reference's default --log-every: its throughput records cover 10 steps
+
+
+def common_config(args, dp, cp):
+    """The workload description both arms print, key for key."""
+    return {"model": Path(args.config).stem, "global_batch": dp, "seq_len": args.length,
+            "parallelism": f"cp{cp}" + (f"xdp{dp}" if dp > 1 else ""),
+            "activation_recompute": bool(args.recompute), "l2": L2_NOTE}
+
+
+def last_window(steps: int) -> int:
+    """Size of the reference's last throughput window over ``steps`` timed steps."""
+    return (steps - 1) % LOG_WINDOW + 1
 
 
 def parse():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--length", type=int, default=8192)
     p.add_argument("--config", default=str(CONFIG))
@@ -205,15 +219,16 @@ def run_ours(args, rank, world, local_rank):
         if graphed:
             # Pinned inputs are copied to the device and the statistics back to
             # pinned memory inside the replayed graph; reading them is the D2H.
-            stats, _ = trainer.step(ids, target, mask, targs.lr * lr_factor(index, targs.steps))
+            trainer.step(ids, target, mask, targs.lr * lr_factor(index, targs.steps))
             d2h = 6 * 8
-            return float(stats[0])
+            stats = trainer.last_stats
+            return float(stats[4] / stats[5])        # global mean loss per supervised token
         trainer.optimizer.zero_grad(set_to_none=True)
         trainer.set_lr(index)
         ids, target, mask = ids.pin_memory(), target.pin_memory(), mask.pin_memory()
         stats = trainer.micro_step(ids, target, mask, last=True)
         trainer.finish_step()
-        loss = float(stats[0])                     # device -> host read of the step's result
+        loss = float(stats[0] / stats[1])          # device -> host read of the step's result (this rank's mean)
         d2h = stats.element_size() * stats.numel()
         return loss
 
@@ -256,17 +271,16 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "strong" if cp > 1 or world == 1 else "weak",
             "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
             "dtype": "bf16", "data": "synthetic (uniform random token ids), random-init weights",
-            "config": {"model": Path(args.config).stem, "global_batch": parallel.dp_size, "seq_len": args.length,
-                       "parallelism": f"cp{cp}" + (f"xdp{parallel.dp_size}" if parallel.dp_size > 1 else ""),
-                       "activation_recompute": bool(args.recompute), "optimizer": "fused AdamW fp32 master",
-                       "l2": "no flush: ~1.3 GB of activations/weights stream per step (> 126 MB L2)",
-                       "ulysses_exchange": "nvlink-fused" if fused_exchange else ("nccl" if cp > 1 else "none"),
-                       "cuda_graph": bool(graphed), "optimizer_shard": bool(targs.optimizer_shard)},
+            "config": common_config(args, parallel.dp_size, cp),
+            "details": {"optimizer": "fused AdamW fp32 master",
+                        "ulysses_exchange": "nvlink-fused" if fused_exchange else ("nccl" if cp > 1 else "none"),
+                        "cuda_graph": bool(graphed), "optimizer_shard": bool(targs.optimizer_shard),
+                        "final_loss_over": f"mean of the last {last_window(args.steps)} steps"},
             "clocks": sampler.summary() if sampler is not None else None,
             "e2e": {"value": round(tokens / wall_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "gpu_launches": int(launches),
-            "final_loss": round(losses[-1] / max(1, args.length // cp), 4),
+            "final_loss": round(sum(losses[-last_window(args.steps):]) / last_window(args.steps), 4),
         }
     if graphed:
         trainer.close()
@@ -293,29 +307,51 @@ def run_reference(args, rank, world, local_rank):
     import st  # noqa: F401  (the reference)
     from st.cli import main as reference_main
     cp = args.cp or world
+    # The reference reports throughput once per 10-step window (its default
+    # --log-every), timed by its host clock after cuda.synchronize and maxed
+    # over ranks. Its warm-up is rounded up to whole windows so that the
+    # windows after it cover exactly the K timed steps.
+    warmup = max(LOG_WINDOW, -(-args.warmup // LOG_WINDOW) * LOG_WINDOW)
     argv = ["train", "--config", str(args.config), "--task", "random", "--length", str(args.length),
             "--batch-size", "1", "--precision", "bf16", "--backend", "auto", "--context-parallel", str(cp),
-            "--steps", str(args.warmup + args.steps), "--log-every", "1", "--save", "", "--eval-every", "0",
+            "--steps", str(warmup + args.steps), "--save", "", "--eval-every", "0",
             "--checkpoint-chunks" if args.recompute else "--no-checkpoint-chunks"]
     buffer = io.StringIO()
+    wall0 = time.perf_counter()
     with contextlib.redirect_stdout(buffer):
         reference_main(argv)
+    wall = time.perf_counter() - wall0
     if rank != 0:
         return None
     records = [json.loads(line) for line in buffer.getvalue().splitlines() if line.startswith("{")]
-    train = [r for r in records if r.get("event") == "train"][-args.steps:]
+    train = [r for r in records if r.get("event") == "train" and r["step"] > warmup]
     dp = world // cp
     tokens_per_step = dp * args.length
-    seconds = sum(tokens_per_step / r["tokens_per_second"] for r in train)
-    value = tokens_per_step * len(train) / seconds
+    steps, seconds, previous = 0, 0.0, warmup
+    for r in train:
+        window = r["step"] - previous
+        previous = r["step"]
+        steps += window
+        seconds += window * tokens_per_step / r["tokens_per_second"]
+    value = tokens_per_step * steps / seconds
+    # Each step's batch is built on the host and copied to the device (ids and
+    # targets int64, mask bool, this rank's shard); the loop reads the token
+    # count, a finiteness flag and the clip norm's finiteness check back.
+    shard = -(-args.length // cp)
     return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": len(train), "warmup": args.warmup, "ms_per_step": round(seconds * 1e3 / len(train), 3),
+            "steps": steps, "warmup": warmup, "ms_per_step": round(seconds * 1e3 / steps, 3),
             "higher_is_better": True, "scaling": "strong" if cp > 1 or world == 1 else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform random token ids), random-init weights",
-            "config": {"model": Path(args.config).stem, "global_batch": dp, "seq_len": args.length,
-                       "parallelism": f"cp{cp}", "activation_recompute": bool(args.recompute),
-                       "timing": "reference's own per-step host clock after cuda.synchronize, max over ranks"},
+            "config": common_config(args, dp, cp),
+            "details": {"timing": "reference's own per-window host clock after cuda.synchronize, max over ranks",
+                        "final_loss_over": f"its last window ({last_window(steps)} steps)",
+                        "process_wall_s": round(wall, 2)},
+            "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": shard * 17 * world,
+                    "d2h_bytes_per_step": 10 * world,
+                    "how": "the reference's host-clock windows, which include its pageable H2D input copies "
+                           "and per-step device-to-host reads"},
+            "final_loss": train[-1]["loss"] if train else None,
             "peak_allocated_gib": train[-1].get("peak_allocated_gib") if train else None}
 
 

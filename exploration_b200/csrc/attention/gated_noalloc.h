@@ -14,7 +14,11 @@
 // 128, block 16/32/64/128. The first call on a device looks up the device
 // address of the scratch array for that device (the device current at the
 // call); make that first call before any stream capture. Returns 0 on success;
-// otherwise writes a message into error_message (if error_capacity > 0).
+// otherwise writes a message into error_message (if error_capacity > 0). A
+// return of 0 means the kernels were enqueued; whether they finished their
+// bounded waits is known only after the stream is synchronised, from
+// eb_gated_attention_bwd_noalloc_status (site != 0: the gradients of that call
+// are incomplete).
 #pragma once
 
 #ifdef __cplusplus
@@ -26,6 +30,11 @@ int eb_gated_attention_bwd_noalloc(const void* grad, const void* q, const void* 
                                    const float* lse, void* dq, void* dk, void* dv, int batch, int queries, int keys,
                                    int heads, int head_dim, int block, void* stream, char* error_message,
                                    int error_capacity);
+
+// Reads and clears the bounded-wait record of the calls above on `device`
+// (*site = 0: no wait gave up; otherwise the wait's site id and *cta the CTA).
+// Call after synchronising. Uses cudaMemcpy/cudaMemset, allocates nothing.
+int eb_gated_attention_bwd_noalloc_status(int device, int* site, int* cta, char* error_message, int error_capacity);
 
 #ifdef __cplusplus
 }

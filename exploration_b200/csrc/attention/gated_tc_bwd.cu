@@ -826,20 +826,34 @@ int noalloc_scratch_address(int device, unsigned char** out, char* msg, int cap)
   return 0;
 }
 
+// The same kernels and warpgroup split as launch_bwd (two gradient warpgroups
+// for gate blocks of at most 64 keys). Returns the first CUDA error of the
+// attribute calls or the launches.
 template <int D, int B>
-void noalloc_launch(const void* grad, const void* q, const void* k, const void* v, int batch, int queries,
-                    int keys, int heads, const BwdParams& params, cudaStream_t stream) {
+cudaError_t noalloc_launch(const void* grad, const void* q, const void* k, const void* v, int batch, int queries,
+                           int keys, int heads, const BwdParams& params, cudaStream_t stream) {
+  constexpr int kSplit = B <= 64 ? 2 : 1;
   CUtensorMap tq = make_bhld_map(const_cast<void*>(q), batch, queries, heads, D, kT);
   CUtensorMap tg = make_bhld_map(const_cast<void*>(grad), batch, queries, heads, D, kT);
   CUtensorMap tk = make_bhld_map(const_cast<void*>(k), batch, keys, heads, D, kT);
   CUtensorMap tv = make_bhld_map(const_cast<void*>(v), batch, keys, heads, D, kT);
   const size_t smem_q = sizeof(DqSmem<D>) + 1024, smem_kv = sizeof(DkvSmem<D>) + 1024;
-  cudaFuncSetAttribute(gated_dq_tc_kernel<D, B, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-  cudaFuncSetAttribute(gated_dkv_tc_kernel<D, B, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-  gated_dq_tc_kernel<D, B, 1><<<dim3((queries + kT - 1) / kT, heads, batch), threads_for(1), smem_q, stream>>>(
-      tq, tg, tk, tv, params);
-  gated_dkv_tc_kernel<D, B, 1><<<dim3((keys + kT - 1) / kT, heads, batch), threads_for(1), smem_kv, stream>>>(
-      tq, tg, tk, tv, params);
+  cudaError_t rc = cudaFuncSetAttribute(gated_dq_tc_kernel<D, B, kSplit>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
+  if (rc != cudaSuccess) return rc;
+  rc = cudaFuncSetAttribute(gated_dkv_tc_kernel<D, B, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
+  if (rc != cudaSuccess) return rc;
+  gated_dq_tc_kernel<D, B, kSplit><<<dim3((queries + kT - 1) / kT, heads, batch), threads_for(kSplit), smem_q,
+                                     stream>>>(tq, tg, tk, tv, params);
+  rc = cudaGetLastError();
+  if (rc != cudaSuccess) return rc;
+  gated_dkv_tc_kernel<D, B, kSplit><<<dim3((keys + kT - 1) / kT, heads, batch), threads_for(kSplit), smem_kv,
+                                      stream>>>(tq, tg, tk, tv, params);
+  return cudaGetLastError();
+}
+
+sm100::ErrorSlot* noalloc_error_slot(unsigned char* base) {
+  return reinterpret_cast<sm100::ErrorSlot*>(base + 2 * kNoAllocRowBytes + kNoAllocBoundBytes);
 }
 
 }  // namespace
@@ -868,6 +882,14 @@ extern "C" int eb_gated_attention_bwd_noalloc(const void* grad, const void* q, c
   }
   if (static_cast<int64_t>(batch) * q_tiles > kNoAllocMaxTiles)
     return noalloc_fail(msg, cap, "batch * ceil(queries/128) exceeds the scratch tile limit", 1);
+  // An error left by earlier work of this thread is not this call's: report it
+  // without launching, and leave it pending for its owner.
+  const cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess) {
+    char text[256];
+    std::snprintf(text, sizeof(text), "a CUDA error is pending from earlier work: %s", cudaGetErrorString(pending));
+    return noalloc_fail(msg, cap, text, 2);
+  }
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
     return noalloc_fail(msg, cap, "no current CUDA device", 2);
@@ -876,7 +898,7 @@ extern "C" int eb_gated_attention_bwd_noalloc(const void* grad, const void* q, c
   auto* delta = reinterpret_cast<float*>(base);
   auto* rho = reinterpret_cast<float*>(base + kNoAllocRowBytes);
   auto* bounds = reinterpret_cast<int*>(base + 2 * kNoAllocRowBytes);
-  auto* err = reinterpret_cast<sm100::ErrorSlot*>(base + 2 * kNoAllocRowBytes + kNoAllocBoundBytes);
+  sm100::ErrorSlot* err = noalloc_error_slot(base);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
   // delta, rho and bounds are fully rewritten below; only the error slot must start at zero.
   if (cudaMemsetAsync(err, 0, sizeof(sm100::ErrorSlot), stream) != cudaSuccess)
@@ -895,16 +917,57 @@ extern "C" int eb_gated_attention_bwd_noalloc(const void* grad, const void* q, c
                    err, queries, keys, heads, q_tiles,
                    static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim))),
                    static_cast<float>(kLog2e / std::sqrt(static_cast<double>(head_dim)))};
+  cudaError_t launched = cudaSuccess;
   try {
 #define EB_NOALLOC_CASE(DD, BB) \
-    if (head_dim == DD && block == BB) noalloc_launch<DD, BB>(grad, q, k, v, batch, queries, keys, heads, params, stream);
+    if (head_dim == DD && block == BB) \
+      launched = noalloc_launch<DD, BB>(grad, q, k, v, batch, queries, keys, heads, params, stream);
     EB_NOALLOC_CASE(64, 16) EB_NOALLOC_CASE(64, 32) EB_NOALLOC_CASE(64, 64) EB_NOALLOC_CASE(64, 128)
     EB_NOALLOC_CASE(128, 16) EB_NOALLOC_CASE(128, 32) EB_NOALLOC_CASE(128, 64) EB_NOALLOC_CASE(128, 128)
 #undef EB_NOALLOC_CASE
   } catch (const std::exception& exc) {   // tensor-map encoding rejected an operand
     return noalloc_fail(msg, cap, exc.what(), 3);
   }
-  const cudaError_t launched = cudaGetLastError();
   if (launched != cudaSuccess) return noalloc_fail(msg, cap, cudaGetErrorString(launched), 2);
   return 0;
+}
+
+// Reads the bounded-wait record of the allocation-free backward on `device`
+// and clears it. The kernels of that entry point give up a wait after about a
+// second (a peer or copy that never arrived); they then stop early, leave
+// dQ/dK/dV incomplete, and record which wait gave up (*site, a WaitSite id,
+// 0 when none did) and in which CTA (*cta). The entry point's return code
+// cannot say so, because the kernels finish after it returns: synchronise the
+// stream of the call, then call this. It copies 8 bytes with cudaMemcpy and
+// clears them with cudaMemset (no allocation), and makes `device` current for
+// the duration of the call. Returns 0, or a nonzero code with a message in
+// error_message when the device is invalid or a copy failed.
+extern "C" int eb_gated_attention_bwd_noalloc_status(int device, int* site, int* cta, char* error_message,
+                                                     int error_capacity) {
+  using namespace eb;
+  if (site == nullptr || cta == nullptr) return noalloc_fail(error_message, error_capacity, "null output", 1);
+  *site = 0;
+  *cta = 0;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count || device >= 64)
+    return noalloc_fail(error_message, error_capacity, "invalid device", 1);
+  int previous = 0;
+  if (cudaGetDevice(&previous) != cudaSuccess) return noalloc_fail(error_message, error_capacity, "no device", 2);
+  if (cudaSetDevice(device) != cudaSuccess) return noalloc_fail(error_message, error_capacity, "cudaSetDevice failed", 2);
+  int rc = 0;
+  unsigned char* base = nullptr;
+  rc = noalloc_scratch_address(device, &base, error_message, error_capacity);
+  if (rc == 0) {
+    sm100::ErrorSlot slot{0, 0};
+    sm100::ErrorSlot* dev_slot = noalloc_error_slot(base);
+    if (cudaMemcpy(&slot, dev_slot, sizeof(slot), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemset(dev_slot, 0, sizeof(slot)) != cudaSuccess) {
+      rc = noalloc_fail(error_message, error_capacity, "reading the error record failed", 2);
+    } else {
+      *site = slot.code;
+      *cta = slot.block;
+    }
+  }
+  cudaSetDevice(previous);
+  return rc;
 }

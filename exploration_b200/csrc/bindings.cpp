@@ -48,6 +48,9 @@ std::vector<at::Tensor> gated_attention_bwd(const at::Tensor& grad, const at::Te
 std::vector<at::Tensor> block_scores_topk(const at::Tensor& q, const at::Tensor& k, const at::Tensor& pos,
                                           int64_t block, int64_t first, int64_t topk);
 bool gemm_supported(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn);
+int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, bool accumulate,
+                   int64_t splits);
+std::vector<int64_t> gemm_plain_plan(int64_t M, int64_t N, int64_t K, int64_t sms);
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
           double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
           const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial);
@@ -136,6 +139,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_pop", &eb::sparse_pop);
   m.def("gemm_supported", &eb::gemm_supported);
   m.def("gemm", &eb::gemm, "persistent tcgen05 GEMM with fused epilogues");
+  m.def("gemm_plain", &eb::gemm_plain, "tcgen05 GEMM without epilogue (store / fp32 accumulate), split-K when few tiles",
+        py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("out"), py::arg("accumulate"),
+        py::arg("splits") = 0);
+  m.def("gemm_plain_plan", &eb::gemm_plain_plan);
   m.def("gemm_scatter", &eb::gemm_scatter, "projection GEMM whose epilogue stores head shards to their owners");
   m.def("gemm_gather", &eb::gemm_gather, "GEMM whose A operand is read from the owners' head shards");
   m.def("heap_alloc", &eb::heap_alloc);

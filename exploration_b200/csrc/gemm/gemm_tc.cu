@@ -78,6 +78,8 @@ struct GemmArgs {
   int64_t ld_aux;
   float* col_partial;      // [tiles_m, N] fp32 partial column sums (kGeluBackBf16)
   float alpha;
+  int splits;              // K split into this many ranges; split s writes out + s * split_stride (fp32 partials)
+  int64_t split_stride;
   int vec;                 // 1: every row start and leading dimension allows 8/16-byte vector access
   ErrorSlot* err;
   PeerLayout peer;
@@ -131,7 +133,8 @@ EB_DEVICE float4 load_bias4(const float* bias, int n, int N) {
 // Four consecutive outputs (m, n..n+3) of one row. Vector accesses need the
 // row start aligned (checked on the host: GemmArgs::vec) and n + 4 <= N.
 template <int EPI>
-EB_DEVICE void epilogue4(const GemmArgs& g, int m, int n, float4 v4, float4 b4, float (&cs)[4], uint2 aux_raw) {
+EB_DEVICE void epilogue4(const GemmArgs& g, int64_t ooff, int m, int n, float4 v4, float4 b4, float (&cs)[4],
+                         uint2 aux_raw) {
   float v[4] = {v4.x, v4.y, v4.z, v4.w};
   const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
   const bool vec = g.vec && n + 4 <= g.N;
@@ -159,7 +162,7 @@ EB_DEVICE void epilogue4(const GemmArgs& g, int m, int n, float4 v4, float4 b4, 
       }
     }
   } else if constexpr (EPI == kStoreF32 || EPI == kAccumF32 || EPI == kBiasResidualF32) {
-    float* o = static_cast<float*>(g.out) + static_cast<int64_t>(m) * g.ldo + n;
+    float* o = static_cast<float*>(g.out) + ooff + static_cast<int64_t>(m) * g.ldo + n;
     const float* res = EPI == kBiasResidualF32 ? g.residual + static_cast<int64_t>(m) * g.ldr + n : nullptr;
     if (vec) {
       if constexpr (EPI == kAccumF32) {
@@ -243,6 +246,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_m = (g.M + kBM - 1) / kBM, tiles_n = (g.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
+  const int units = tiles * g.splits;     // (split, tile) pairs; consecutive units share a K range
   const int k_blocks = (g.K + kBK - 1) / kBK;
   volatile int* abort = &sm.abort;
   if (threadIdx.x == 0) {
@@ -273,10 +277,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       prefetch_tensormap(&tb);
       int it = 0;   // global k-slice counter across tiles
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x) {
+        const int split = unit / tiles, tile = unit - split * tiles;
         int tm, tn;
         tile_coords(tile, tiles_m, tiles_n, tm, tn);
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        const int kb0 = split * k_blocks / g.splits, kb1 = (split + 1) * k_blocks / g.splits;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1, abort, g.err, kSiteGemm)) {
             ok = false;
@@ -313,12 +319,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       const uint32_t idesc = idesc_bf16(kBM, BN, A_MN, B_MN);
       int it = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x, ++local) {
+        const int split = unit / tiles;
+        const int kb0 = split * k_blocks / g.splits, kb1 = (split + 1) * k_blocks / g.splits;
         const int acc = local & 1;
         if (local >= 2 && !mbar_wait(&sm.acc_empty[acc], ((local >> 1) - 1) & 1, abort, g.err, kSiteGemm)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&sm.full[s], (it / kStages) & 1, abort, g.err, kSiteGemm)) {
             ok = false;
@@ -332,7 +340,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                                      : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t db = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 64 * kBK * 2, 1024)
                                      : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            mma_ss(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&sm.empty[s]);
         }
@@ -351,7 +359,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     float4* stage = sm.stage[ew];
     const int rq = lane >> 2, u = lane & 3;
     int local = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++local) {
+      const int split = unit / tiles, tile = unit - split * tiles;
+      const int64_t ooff = static_cast<int64_t>(split) * g.split_stride;
       int tm, tn;
       tile_coords(tile, tiles_m, tiles_n, tm, tn);
       const int acc = local & 1;
@@ -433,7 +443,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             const int rr = it * 8 + rq;
             const float4 v = stage[rr * 4 + (u ^ ((rr >> 1) & 3))];
             const int m = tm * kBM + wr * 32 + rr;
-            if (m < g.M && n < g.N) epilogue4<EPI>(g, m, n, v, bias4, cs, aux_raw[half][it]);
+            if (m < g.M && n < g.N) epilogue4<EPI>(g, ooff, m, n, v, bias4, cs, aux_raw[half][it]);
           }
           __syncwarp();
           if constexpr (EPI == kGeluBackBf16) {
@@ -479,15 +489,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   }
 }
 
+int sm_count(int device) {
+  static int cached[64] = {0};
+  if (device < 0 || device >= 64) device = 0;
+  if (cached[device] == 0) {
+    int sms = 0;
+    EB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    cached[device] = sms;
+  }
+  return cached[device];
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A>
 void launch_gemm(const CUtensorMap& ta, const PeerMaps& pm, const at::Tensor& b, int M, int N, int K,
                  GemmArgs& args, cudaStream_t stream) {
   CUtensorMap tb = B_MN ? make_matrix_map(b.data_ptr(), K, N, b.stride(0), kBK)   // [K, N], box 64n x 64k
                         : make_matrix_map(b.data_ptr(), N, K, b.stride(0), BN);   // [N, K], box 64k x BN n
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  int sms = 0;
-  EB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b.device().index()));
-  const int grid = std::min(tiles, sms);
+  const int units = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * std::max(1, args.splits);
+  const int grid = std::min(units, sm_count(b.device().index()));
   const size_t smem = sizeof(GemmSmem<BN>) + 1024;
   auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, EPI, GATHER_A>;
   EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -510,20 +529,85 @@ bool wide_tiles(int M, int N) {
   return N >= 256 && tiles256 >= 148;
 }
 
+// bn: output tile width, 0 = chosen from the problem size.
 template <bool A_MN, bool B_MN, int EPI>
 void dispatch_bn(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args,
-                 cudaStream_t stream) {
-  if (wide_tiles(M, N)) run_gemm<256, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
+                 cudaStream_t stream, int bn) {
+  if (bn == 256 || (bn == 0 && wide_tiles(M, N))) run_gemm<256, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
   else run_gemm<128, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
 }
 
 template <int EPI>
 void dispatch_layout(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int M, int N, int K,
-                     GemmArgs& args, cudaStream_t stream) {
-  if (!a_mn && !b_mn) dispatch_bn<false, false, EPI>(a, b, M, N, K, args, stream);
-  else if (!a_mn && b_mn) dispatch_bn<false, true, EPI>(a, b, M, N, K, args, stream);
-  else if (a_mn && !b_mn) dispatch_bn<true, false, EPI>(a, b, M, N, K, args, stream);
-  else dispatch_bn<true, true, EPI>(a, b, M, N, K, args, stream);
+                     GemmArgs& args, cudaStream_t stream, int bn = 0) {
+  if (!a_mn && !b_mn) dispatch_bn<false, false, EPI>(a, b, M, N, K, args, stream, bn);
+  else if (!a_mn && b_mn) dispatch_bn<false, true, EPI>(a, b, M, N, K, args, stream, bn);
+  else if (a_mn && !b_mn) dispatch_bn<true, false, EPI>(a, b, M, N, K, args, stream, bn);
+  else dispatch_bn<true, true, EPI>(a, b, M, N, K, args, stream, bn);
+}
+
+// Sums the split partials ws[0..splits) in split order (so the result does
+// not depend on which CTA finished first) and stores (or adds) them into the
+// contiguous output. Four consecutive elements per thread.
+template <bool kBf16Out>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float4* __restrict__ ws, int splits, int64_t n4,
+                                                            int64_t stride4, void* __restrict__ out, int accumulate) {
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += step) {
+    float4 acc = ws[i];
+    for (int s = 1; s < splits; ++s) {
+      const float4 p = ws[s * stride4 + i];
+      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    if constexpr (kBf16Out) {
+      static_cast<uint2*>(out)[i] = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+    } else {
+      float4* o = static_cast<float4*>(out) + i;
+      if (accumulate) {
+        const float4 old = *o;
+        acc.x = old.x + acc.x; acc.y = old.y + acc.y; acc.z = old.z + acc.z; acc.w = old.w + acc.w;
+      }
+      *o = acc;
+    }
+  }
+}
+
+struct GemmPlan {
+  int bn;
+  int splits;
+};
+
+// Tile width and K split of a GEMM without a fused epilogue, from a small cost
+// model in units of one 128 x 128 x 64 MMA step: waves x (k-blocks per unit x
+// tile width + the tile's epilogue), plus, when K is split, the partials'
+// round trip through L2 (written once, read once, and the output). Narrow
+// tiles run about 15% below wide ones per FLOP (twice the B traffic per FLOP).
+// Weight gradients (M, N <= a few thousand, K = tokens) are the shapes that
+// split; token-major GEMMs have enough tiles without it.
+GemmPlan plan_plain(int M, int N, int K, int sms, bool can_split) {
+  const int k_blocks = (K + kBK - 1) / kBK;
+  constexpr double kStepSeconds = 256.0 / 1.9e9;   // one 128x128x64 step at ~8K FLOP/clock
+  constexpr double kPartialBandwidth = 8e12;        // partials stay in L2 between the two kernels
+  GemmPlan best{N >= 256 ? 256 : 128, 1};
+  double best_t = 1e300;
+  for (int bn : {256, 128}) {
+    if (bn == 256 && N < 256) continue;
+    const long tiles = static_cast<long>((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+    const int max_split = can_split ? std::max(1, std::min(16, k_blocks / 4)) : 1;
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const long units = tiles * sp;
+      const long waves = (units + sms - 1) / sms;
+      const double kb = static_cast<double>((k_blocks + sp - 1) / sp);
+      const double unit_t = kb * (bn / 128.0) * (bn == 128 ? 1.15 : 1.0) + 2.0 * bn / 128.0;
+      double t = static_cast<double>(waves) * unit_t;
+      if (sp > 1) t += (sp + 2.0) * M * static_cast<double>(N) * 4.0 / kPartialBandwidth / kStepSeconds;
+      if (t < best_t * 0.97) {
+        best_t = t;
+        best = GemmPlan{bn, sp};
+      }
+    }
+  }
+  return best;
 }
 
 bool aligned16(const at::Tensor& t) {
@@ -550,6 +634,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
   TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "gemm: bad output");
   const c10::cuda::CUDAGuard guard(a.device());
   GemmArgs args{};
+  args.splits = 1;
   args.M = M;
   args.N = N;
   args.K = K;
@@ -621,6 +706,7 @@ PeerLayout make_layout(int64_t world, int64_t rank, int64_t parts, int64_t batch
 
 GemmArgs base_args(int M, int N, int K, const at::Tensor& ref) {
   GemmArgs args{};
+  args.splits = 1;
   args.M = M;
   args.N = N;
   args.K = K;
@@ -734,6 +820,74 @@ void gemm_gather(const std::vector<int64_t>& src, int64_t rank, int64_t parts, i
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(1);
+}
+
+// out = op(A) op(B)^T (store) or out += op(A) op(B)^T (accumulate, fp32 out)
+// with no fused epilogue: the linear layers' plain forwards (bf16 or fp32
+// logits), their input gradients (dx = dy W, B MN-major) and their weight
+// gradients (dW = dy^T x, both operands MN-major, accumulated into the fp32
+// gradient). Few-tile shapes split K: fp32 partials of each split go to a
+// workspace and one reduce kernel sums them in a fixed order (deterministic,
+// no atomics) into the output. `splits`: 0 = chosen by the cost model.
+// Returns the split count used.
+int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, bool accumulate,
+                   int64_t splits) {
+  TORCH_CHECK(gemm_supported(a, a_mn, b, b_mn), "gemm_plain: bf16 2-D operands with 16-byte aligned rows required");
+  const int M = a_mn ? a.size(1) : a.size(0);
+  const int K = a_mn ? a.size(0) : a.size(1);
+  const int N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm_plain: inner dimensions differ");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "gemm_plain: bad output");
+  const bool bf16_out = out.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf16_out || out.scalar_type() == at::kFloat, "gemm_plain: bf16 or fp32 output");
+  TORCH_CHECK(!(accumulate && bf16_out), "gemm_plain: accumulation needs an fp32 output");
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int sms = sm_count(a.device().index());
+  const int k_blocks = (K + kBK - 1) / kBK;
+  // The reduce kernel reads and writes four contiguous elements at a time.
+  const bool can_split = out.is_contiguous() && N % 4 == 0 &&
+                         reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0 && k_blocks >= 2;
+  GemmPlan plan = plan_plain(M, N, K, sms, can_split);
+  if (splits > 0) plan.splits = can_split ? static_cast<int>(std::min<int64_t>(splits, k_blocks)) : 1;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  GemmArgs args = base_args(M, N, K, a);
+  args.ldo = out.stride(0);
+  if (plan.splits == 1) {
+    args.out = out.data_ptr();
+    args.vec = (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0 && (args.ldo * out.element_size()) % 16 == 0;
+    if (bf16_out) dispatch_layout<kStoreBf16>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
+    else if (accumulate) dispatch_layout<kAccumF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
+    else dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch(1);
+    return 1;
+  }
+  auto ws = at::empty({plan.splits, static_cast<int64_t>(M), static_cast<int64_t>(N)}, out.options().dtype(at::kFloat));
+  args.out = ws.data_ptr();
+  args.ldo = N;
+  args.splits = plan.splits;
+  args.split_stride = static_cast<int64_t>(M) * N;
+  args.vec = 1;
+  dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t n4 = static_cast<int64_t>(M) * N / 4;
+  const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8));
+  if (bf16_out)
+    splitk_reduce_kernel<true><<<grid, 256, 0, stream>>>(reinterpret_cast<const float4*>(ws.data_ptr()),
+                                                         plan.splits, n4, n4, out.data_ptr(), 0);
+  else
+    splitk_reduce_kernel<false><<<grid, 256, 0, stream>>>(reinterpret_cast<const float4*>(ws.data_ptr()),
+                                                          plan.splits, n4, n4, out.data_ptr(), accumulate ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch(2);
+  return plan.splits;
+}
+
+// The plan gemm_plain would use: (tile width, splits), for tests and tools.
+std::vector<int64_t> gemm_plain_plan(int64_t M, int64_t N, int64_t K, int64_t sms) {
+  const GemmPlan plan = plan_plain(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                   static_cast<int>(sms), N % 4 == 0 && (K + kBK - 1) / kBK >= 2);
+  return {plan.bn, plan.splits};
 }
 
 int64_t gemm_tile_m() { return kBM; }

@@ -1,10 +1,13 @@
 """Linear layers on the persistent tcgen05 GEMM (``csrc/gemm/gemm_tc.cu``).
 
 The kernel reads either operand K-major or MN-major, so every GEMM of a
-layer runs without a transpose copy. GEMMs that carry an epilogue run on
-it; plain ones with no fusion (``dx = dy W`` and the weight gradients
-``dW = dy^T x`` in fp32) are library GEMMs. The fused layers keep
-elementwise work inside the GEMM epilogues:
+layer runs on it without a transpose copy: the forward ``y = x W^T``, the
+input gradient ``dx = dy W`` (W read MN-major) and the weight gradient
+``dW = dy^T x`` (both operands MN-major), which is added straight into the
+fp32 gradient. Weight gradients have few output tiles and a long reduction
+(the tokens), so the kernel splits K across CTAs there and one reduce kernel
+sums the fp32 partials in a fixed order (deterministic). The fused layers
+keep elementwise work inside the GEMM epilogues:
 
 * ``linear_residual``: ``out = residual + x W^T (+ b)`` in fp32 (the residual
   stream update), one kernel instead of GEMM + add;
@@ -47,14 +50,33 @@ def gemm(a, a_mn, b, b_mn, out, epilogue, alpha=1.0, bias=None, residual=None, a
     return out
 
 
-def weight_grad(g, x):
-    """``dW = g^T x`` in fp32: a plain GEMM with no epilogue, left to cuBLAS.
+def plain(a, a_mn, b, b_mn, out, accumulate=False, splits=0):
+    """``out (+)= op(A) op(B)^T`` with no epilogue (split-K when the output has few tiles)."""
+    ext = _native.native(a)
+    used = ext.gemm_plain(a, a_mn, b, b_mn, out, accumulate, splits)
+    record("gemm_tc", epilogue="accumulate" if accumulate else "store", a_mn=a_mn, b_mn=b_mn, splits=used)
+    return out
 
-    Weight gradients have few output tiles and a long reduction (tokens), a
-    shape where cuBLAS's split reduction is faster than this kernel's
-    one-tile-per-CTA schedule.
-    """
-    return torch.mm(g.t(), x, out_dtype=torch.float32)
+
+def forward(x2, w, out_f32=False):
+    """``x W^T`` (x [T, K], W [N, K]), bf16 or fp32 output."""
+    out = torch.empty(x2.shape[0], w.shape[0], device=x2.device,
+                      dtype=torch.float32 if out_f32 else torch.bfloat16)
+    return plain(x2, False, w, False, out)
+
+
+def input_grad(g, w):
+    """``dx = g W`` (g [T, N], W [N, K]; W read MN-major), bf16."""
+    out = torch.empty(g.shape[0], w.shape[1], device=g.device, dtype=torch.bfloat16)
+    return plain(g, False, w, True, out)
+
+
+def weight_grad(g, x, out=None):
+    """``dW = g^T x`` in fp32 (g [T, N], x [T, K]: both read MN-major); added into ``out`` when given."""
+    if out is None:
+        out = torch.empty(g.shape[1], x.shape[1], device=g.device, dtype=torch.float32)
+        return plain(g, True, x, True, out)
+    return plain(g, True, x, True, out, accumulate=True)
 
 
 # id(param) -> (weak reference to param, callback). A registered parameter
@@ -80,8 +102,7 @@ def accumulate_weight_grad(param, g, x):
     sink = _grad_sinks.get(id(param)) if param is not None else None
     if (sink is not None and sink[0]() is param and g.is_cuda and param.grad is not None
             and param.grad.dtype == torch.float32 and param.grad.is_contiguous()):
-        grad = param.grad.view(param.shape)
-        torch.addmm(grad, g.t(), x, out_dtype=torch.float32, out=grad)
+        weight_grad(g, x, out=param.grad.view(param.shape))
         sink[1](param)
         return None
     return weight_grad(g, x)
@@ -143,11 +164,11 @@ class Linear(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, weight, out_f32):
-        # No epilogue to fuse: a library GEMM (fp32 output straight from bf16
-        # operands when asked, e.g. for the logits).
+        # No epilogue to fuse (fp32 output straight from the accumulator when
+        # asked, e.g. for the logits).
         x2 = _flat(x)
         w = _bf16_weight(weight)
-        out = torch.mm(x2, w.t(), out_dtype=torch.float32) if out_f32 else torch.mm(x2, w.t())
+        out = forward(x2, w, out_f32)
         ctx.save_for_backward(x2, w)
         ctx.shape = x.shape
         ctx.param = weight
@@ -158,7 +179,7 @@ class Linear(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w = ctx.saved_tensors
         g = _flat(dy).to(torch.bfloat16)
-        dx = g @ w
+        dx = input_grad(g, w)
         return dx.view(ctx.shape), accumulate_weight_grad(ctx.param, g, x2), None
 
 
@@ -189,7 +210,7 @@ class LinearResidual(torch.autograd.Function):
             g, db = cast_colsum(d32, ctx.bias)
         else:
             g, db = d32.to(torch.bfloat16), None
-        dx = g @ w
+        dx = input_grad(g, w)
         dw = accumulate_weight_grad(ctx.param, g, x2)
         return dx.view(ctx.shape), dw, db, hand_residual(ctx.link, dout), None
 
@@ -227,7 +248,7 @@ class FFNResidual(torch.autograd.Function):
         gemm(g, False, w2b, True, dh_pre, GELU_BACK, aux=dgelu, partial=partial)
         db1 = column_sum(partial, ctx.biases[0])
         dw1 = accumulate_weight_grad(ctx.params[0], dh_pre, h2)
-        dh = dh_pre @ w1b
+        dh = input_grad(dh_pre, w1b)
         return dh.view(ctx.shape), hand_residual(ctx.link, dout), dw1, db1, dw2, db2, None
 
 

@@ -93,7 +93,7 @@ class _ProjectToHeads(torch.autograd.Function):
         if gather_mode() == "fused":
             U.ext.gemm_gather(ptrs, U.rank, parts, batch, n_local, C, w, True, dx, G.STORE_BF16, None, None)
         else:
-            G.gemm(dy_seq, False, w, True, dx, G.STORE_BF16)
+            G.plain(dy_seq, False, w, True, dx)
         dw = G.accumulate_weight_grad(ctx.param, dy_seq, x2)
         return dx.view(shape), dw, None, None, None, None
 

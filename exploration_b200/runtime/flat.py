@@ -670,6 +670,7 @@ class GraphTrainer:
         if self.cuda:
             torch.cuda.current_stream().synchronize()
         stats = stats_host.clone()          # [loss_sum, count, correct, grad_sq_norm, global loss, global count]
+        self.last_stats = stats
         if stats[5] == 0:
             self.optimizer.step_count -= 1
             raise ValueError("global batch has no supervised tokens")

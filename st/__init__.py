@@ -32,7 +32,7 @@ def _alias_all():
         sys.modules["st." + info.name[len(prefix):]] = module
     for alias, target in _LEGACY.items():
         sys.modules["st." + alias] = importlib.import_module(prefix + target)
-    for name in ("models", "ops", "runtime", "data", "tools", "parallel", "utils", "cli", "config",
+    for name in ("models", "ops", "runtime", "data", "tools", "parallel", "cli", "config",
                  "api"):
         globals()[name] = sys.modules["st." + name]
     for alias in ("blocks", "stack_model", "baseline", "attention", "sparse", "flash", "checkpoint",

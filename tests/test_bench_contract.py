@@ -44,3 +44,32 @@ def test_clock_sampler_without_samples():
     sampler = _bench().ClockSampler([0])
     sampler.mark(0.0, 1.0)
     assert sampler.summary()["reasons"] == ["unsampled"]
+
+
+def test_gemm_plan_splits_only_few_tile_shapes():
+    """Weight-gradient shapes (few output tiles, K = tokens) split K; token-major GEMMs do not."""
+    from exploration_b200.ops import _native
+    ext = _native.load(required=False)
+    if ext is None:
+        import pytest
+        pytest.skip("extension not built")
+    assert ext.gemm_plain_plan(1024, 1024, 8192, 148)[1] > 1
+    assert ext.gemm_plain_plan(256, 1024, 8192, 148)[1] > 1
+    assert ext.gemm_plain_plan(8192, 1024, 3072, 148) == [256, 1]
+    assert ext.gemm_plain_plan(4096, 1024, 8192, 148)[1] == 1
+    bn, splits = ext.gemm_plain_plan(8192, 4096, 64, 148)
+    assert splits == 1
+
+
+def test_both_arms_describe_the_workload_with_the_same_keys():
+    bench = _bench()
+
+    class Args:
+        config = str(ROOT / "configs" / "stack_100m.json")
+        length = 8192
+        recompute = False
+
+    ours = bench.common_config(Args, 1, 2)
+    assert set(ours) == {"model", "global_batch", "seq_len", "parallelism", "activation_recompute", "l2"}
+    assert ours["parallelism"] == "cp2" and ours["model"] == "stack_100m"
+    assert [bench.last_window(k) for k in (1, 10, 20, 25, 100)] == [1, 10, 10, 5, 10]

@@ -94,3 +94,68 @@ def test_fused_layers_match_torch():
     for a, e in zip(got, want):
         scale = max(1.0, e.abs().max().item())
         torch.testing.assert_close(a.float(), e, atol=5e-2 * scale, rtol=5e-2)
+
+
+@pytest.mark.parametrize("n_out,k_in", [(1024, 1024), (256, 1024), (3072, 1024), (200, 136)])
+@pytest.mark.parametrize("splits", [0, 1, 5])
+def test_weight_grad_accumulates_over_long_reductions(n_out, k_in, splits):
+    """``dW += g^T x`` at the training reduction length (8,192 tokens), both operands MN-major."""
+    tokens = 8192
+    g, _ = _operand(tokens, n_out, False, 7)
+    x, _ = _operand(tokens, k_in, False, 8)
+    grad = torch.randn(n_out, k_in, device="cuda")
+    start = grad.clone()
+    G.plain(g, True, x, True, grad, accumulate=True, splits=splits)
+    want = start + g.float().t() @ x.float()
+    torch.testing.assert_close(grad, want, atol=5e-2, rtol=2e-3)
+
+
+def test_weight_grad_split_k_is_deterministic(native):
+    g, _ = _operand(8192, 1024, False, 9)
+    x, _ = _operand(8192, 1024, False, 10)
+    assert native.gemm_plain_plan(1024, 1024, 8192, torch.cuda.get_device_properties(0).multi_processor_count)[1] > 1
+    first = G.weight_grad(g, x)
+    for _ in range(3):
+        assert torch.equal(G.weight_grad(g, x), first)
+
+
+@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("m,n,k", [(8192, 1024, 3072), (1000, 256, 1024), (384, 520, 4096)])
+def test_forward_and_input_grad(m, n, k, splits):
+    """``x W^T`` (bf16 / fp32 out) and ``dy W`` (W read MN-major) against fp32 torch."""
+    x, _ = _operand(m, k, False, 11)
+    w, _ = _operand(n, k, False, 12)
+    ref = x.float() @ w.float().t()
+    out32 = torch.empty(m, n, device="cuda")
+    G.plain(x, False, w, False, out32, splits=splits)
+    torch.testing.assert_close(out32, ref, atol=5e-2, rtol=2e-3)
+    out16 = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    G.plain(x, False, w, False, out16, splits=splits)
+    torch.testing.assert_close(out16.float(), ref, atol=0.25, rtol=2e-2)
+    dy, _ = _operand(m, n, False, 13)
+    w2, _ = _operand(n, k, False, 14)
+    dx = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
+    G.plain(dy, False, w2, True, dx, splits=splits)
+    torch.testing.assert_close(dx.float(), dy.float() @ w2.float(), atol=0.25, rtol=2e-2)
+
+
+def test_linear_layer_runs_no_library_gemm():
+    """The no-bias linear layer (QKV, projections, LM head) runs forward and backward on gemm_tc."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.manual_seed(1)
+    layer = torch.nn.Linear(1024, 3072, bias=False).cuda()
+    x = torch.randn(4096, 1024, device="cuda").to(torch.bfloat16).requires_grad_()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        y = G.Linear.apply(x, layer.weight, False)
+        y.float().square().sum().backward()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert any("gemm_tc_kernel" in n for n in names)
+    library = [n for n in names if n.startswith(("nvjet", "cutlass", "sm90_", "sm100_"))
+               or ("gemm" in n.lower() and "gemm_tc" not in n)]
+    assert not library, library
+    xr = x.detach().float().requires_grad_()
+    want = xr @ layer.weight.t()
+    torch.testing.assert_close(y.float(), want, atol=0.25, rtol=2e-2)
+    (want.square().sum()).backward()
+    torch.testing.assert_close(x.grad.float(), xr.grad, atol=1.0, rtol=3e-2)

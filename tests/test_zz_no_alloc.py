@@ -27,6 +27,24 @@ def entry_point():
     return fn
 
 
+def status_reader():
+    lib = ctypes.CDLL(str(_native.so_path()))
+    fn = lib.eb_gated_attention_bwd_noalloc_status
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), ctypes.c_char_p,
+                   ctypes.c_int]
+    return fn
+
+
+def wait_record(device):
+    """(site, cta) of a bounded wait of the allocation-free kernels that gave up; (0, 0) when none did."""
+    site, cta = ctypes.c_int(-1), ctypes.c_int(-1)
+    message = ctypes.create_string_buffer(256)
+    status = status_reader()(device, ctypes.byref(site), ctypes.byref(cta), message, len(message))
+    assert status == 0, message.value.decode()
+    return site.value, cta.value
+
+
 def forward_case(seed, batch, queries, keys, heads, dim, block):
     ext = _native.load(required=True)
     g = torch.Generator(device="cuda").manual_seed(seed)
@@ -51,7 +69,8 @@ def call(fn, tensors, dq, dk, dv, batch, queries, keys, heads, dim, block):
 
 def test_noalloc_backward_matches_regular_entry_point_twice(native):
     fn = entry_point()
-    cases = [(11, 1, 300, 640, 3, 64, 16), (12, 2, 200, 520, 2, 128, 128)]
+    # One warpgroup split (block <= 64: two gradient warpgroups) and one without, at both head sizes.
+    cases = [(11, 1, 300, 640, 3, 64, 16), (12, 2, 200, 520, 2, 128, 128), (13, 1, 260, 700, 2, 128, 32)]
     for seed, batch, queries, keys, heads, dim, block in cases:
         ext, tensors = forward_case(seed, batch, queries, keys, heads, dim, block)
         want = ext.gated_attention_bwd(*tensors, block)
@@ -59,9 +78,9 @@ def test_noalloc_backward_matches_regular_entry_point_twice(native):
         status, message = call(fn, tensors, dq, dk, dv, batch, queries, keys, heads, dim, block)
         assert status == 0, message
         torch.cuda.synchronize()
+        assert wait_record(torch.cuda.current_device()) == (0, 0)
         for name, got, ref in zip(("dq", "dk", "dv"), (dq, dk, dv), want):
             torch.testing.assert_close(got.float(), ref.float(), atol=ATOL, rtol=RTOL, msg=name)
-    assert native.device_errors(torch.cuda.current_device()) == (0, 0)
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
