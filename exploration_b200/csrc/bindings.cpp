@@ -49,11 +49,11 @@ std::vector<at::Tensor> block_scores_topk(const at::Tensor& q, const at::Tensor&
                                           int64_t block, int64_t first, int64_t topk);
 bool gemm_supported(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn);
 int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, bool accumulate,
-                   int64_t splits);
+                   int64_t splits, int64_t shape);
 std::vector<int64_t> gemm_plain_plan(int64_t M, int64_t N, int64_t K, int64_t sms);
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
           double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
-          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial);
+          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial, int64_t shape);
 void gemm_scatter(const at::Tensor& a, const at::Tensor& b, bool b_mn, const std::vector<int64_t>& dst,
                   int64_t rank, int64_t parts, int64_t batch, int64_t n_local, int64_t C);
 void gemm_gather(const std::vector<int64_t>& src, int64_t rank, int64_t parts, int64_t batch, int64_t n_local,
@@ -138,10 +138,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("block_scores_topk", &eb::block_scores_topk);
   m.def("sparse_pop", &eb::sparse_pop);
   m.def("gemm_supported", &eb::gemm_supported);
-  m.def("gemm", &eb::gemm, "persistent tcgen05 GEMM with fused epilogues");
+  m.def("gemm", &eb::gemm, "persistent tcgen05 GEMM with fused epilogues", py::arg("a"), py::arg("a_mn"),
+        py::arg("b"), py::arg("b_mn"), py::arg("out"), py::arg("epilogue"), py::arg("alpha"), py::arg("bias"),
+        py::arg("residual"), py::arg("aux"), py::arg("col_partial"), py::arg("shape") = 0);
   m.def("gemm_plain", &eb::gemm_plain, "tcgen05 GEMM without epilogue (store / fp32 accumulate), split-K when few tiles",
         py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("out"), py::arg("accumulate"),
-        py::arg("splits") = 0);
+        py::arg("splits") = 0, py::arg("shape") = 0);
   m.def("gemm_plain_plan", &eb::gemm_plain_plan);
   m.def("gemm_scatter", &eb::gemm_scatter, "projection GEMM whose epilogue stores head shards to their owners");
   m.def("gemm_gather", &eb::gemm_gather, "GEMM whose A operand is read from the owners' head shards");

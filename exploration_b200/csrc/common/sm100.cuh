@@ -126,6 +126,15 @@ EB_DEVICE void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int
                : "memory");
 }
 
+// Tiled TMA reduction: adds a shared-memory box into global memory element by
+// element (fp32 add, in the tensor map's type), tracked by the bulk-async group.
+EB_DEVICE void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 EB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // The committed stores have finished reading shared memory (the source may be reused).
@@ -246,6 +255,76 @@ EB_DEVICE void tmem_st32(uint32_t addr, const uint32_t (&r)[32]) {
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
       "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
       "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// CTA pairs (cta_group::2): two CTAs of a 2-CTA cluster share one MMA whose
+// A rows and B columns are split between their shared memories and whose
+// accumulator rows are split between their TMEMs. The even CTA (rank 0)
+// issues the MMAs; every barrier that the MMA waits on lives in its shared
+// memory. Loads are plain tiled TMA loads of this GPU's memory into the
+// issuing CTA; only their completion is signalled on the leader's barrier.
+// ---------------------------------------------------------------------------
+
+EB_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of both CTAs; orders shared-memory writes (barrier inits) before the peer uses them.
+EB_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of the object at this CTA's `ptr` offset in CTA `rank` of the cluster.
+EB_DEVICE uint32_t cluster_addr(const void* ptr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(ptr)), "r"(rank));
+  return out;
+}
+
+// One arrival on an mbarrier of another CTA of the cluster (release at cluster scope).
+EB_DEVICE void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Tiled 2-D load into this CTA's shared memory whose byte count completes on
+// `cluster_bar`, a barrier of either CTA of the pair (here: the leader's).
+EB_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+
+// Warp-wide, in the same warp of both CTAs: `cols` TMEM columns at the same
+// address in both TMEMs (written to *slot in each CTA).
+EB_DEVICE void tmem_alloc_pair(uint32_t* slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+
+EB_DEVICE void tmem_dealloc_pair(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+}
+
+// Arrive on the barrier at `cluster_bar` (either CTA of the pair) once every
+// pair MMA issued so far by this thread completes.
+EB_DEVICE void tc_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// Pair MMA: D[tmem of both CTAs] (+)= A[both smems] * B[both smems]^T, kind::f16.
+EB_DEVICE void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

@@ -114,6 +114,31 @@ inline CUtensorMap make_store_plane_map(const void* base, int64_t planes, int64_
   return map;
 }
 
+// GEMM output [planes, rows, cols] (cols contiguous, row stride `ld` elements,
+// plane stride `plane` elements; fp32 or bf16) for TMA stores / reductions of
+// 32-row boxes whose rows are one swizzle span wide: 128 bytes (32 fp32 columns,
+// 128-byte swizzle) for fp32, 64 bytes (32 bf16 columns, 64-byte swizzle) for bf16.
+inline CUtensorMap make_epilogue_map(const void* base, int64_t planes, int64_t rows, int64_t cols, int64_t ld,
+                                     int64_t plane, bool fp32) {
+  bind_primary_context();
+  const int elem = fp32 ? 4 : 2;
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * elem) % 16 == 0 && (plane * elem) % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * elem, static_cast<cuuint64_t>(plane) * elem};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t unit[3] = {1, 1, 1};
+  CUresult res = tensor_map_encoder()(&map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                      3, const_cast<void*>(base), dims, strides, box, unit,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(res == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", static_cast<int>(res));
+  return map;
+}
+
 // One error slot per device, allocated on first use and kept for the process
 // (defined in attention/gated_entry.cu).
 sm100::ErrorSlot* device_error_slot(int device);

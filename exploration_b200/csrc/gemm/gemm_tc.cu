@@ -7,11 +7,16 @@
 // GEMMs), so all three GEMMs of a linear layer (y = x W^T, dx = dy W,
 // dW = dy^T x) run without a transpose copy.
 //
-// CTA = one SM, persistent over 128 x BN output tiles (grouped order for
-// L2 reuse). Warp 0 streams A/B k-slices (64 deep, 128-byte swizzle) through
-// a 4-stage TMA ring; warp 1 issues tcgen05.mma (M=128, N=BN, K=16) into one
-// of two TMEM accumulators; warps 4-7 drain the other accumulator (thread =
-// output row) through the fused epilogue while the next tile accumulates.
+// Persistent over (128 * CTAS) x BN output tiles (grouped order for L2
+// reuse). With CTAS = 1 a CTA owns an SM and a 128 x BN tile. With CTAS = 2 a
+// 2-CTA cluster runs one cta_group::2 MMA of 256 x BN: each CTA stages its 128
+// rows of A and BN/2 columns of B, so an SM holds half the B tile (half the
+// shared-memory traffic per FLOP of the single-CTA form) and keeps 6 stages in
+// flight; the even CTA issues the MMAs and both CTAs drain their 128
+// accumulator rows. Warp 0 streams A/B k-slices (64 deep, 128-byte swizzle)
+// through the TMA ring; warp 1 issues tcgen05.mma (K=16) into one of two TMEM
+// accumulators; warps 4-11 drain the other accumulator (thread = output row)
+// through the fused epilogue while the next tile accumulates.
 //
 // Epilogues: bf16 store | fp32 store | fp32 accumulate-into (weight grads) |
 // bias + exact GELU -> bf16 (gelu'(pre-activation) kept for backward) |
@@ -67,6 +72,12 @@ struct PeerMaps {
   CUtensorMap map[kMaxPeers];      // gather sources or scatter targets, one 3-D map per rank
 };
 
+// Targets of the TMA epilogue: the output [planes, M, N] (planes = K splits)
+// and, for bias+GELU, the kept derivative [M, N]; 32 x 32 boxes (make_epilogue_map).
+struct OutMaps {
+  CUtensorMap out, aux;
+};
+
 struct GemmArgs {
   int M, N, K;
   void* out;
@@ -81,20 +92,33 @@ struct GemmArgs {
   int splits;              // K split into this many ranges; split s writes out + s * split_stride (fp32 partials)
   int64_t split_stride;
   int vec;                 // 1: every row start and leading dimension allows 8/16-byte vector access
+  int tma_out;             // 1: the epilogue writes through shared memory with TMA (OutMaps hold the targets)
   ErrorSlot* err;
   PeerLayout peer;
 };
 
-template <int BN>
+template <int BN, int CTAS>
+struct GemmShape {
+  static constexpr int kTileM = kBM * CTAS;                   // rows of one output tile
+  static constexpr int kBNc = BN / CTAS;                      // B rows (n) staged by each CTA
+  static constexpr int kStagesN = CTAS == 2 ? 6 : kStages;
+  static constexpr uint32_t kStageBytes = (kBM + kBNc) * kBK * 2;   // per CTA
+};
+
+template <int BN, int CTAS>
 struct alignas(1024) GemmSmem {
-  __nv_bfloat16 a[kStages][kBM * kBK];
-  __nv_bfloat16 b[kStages][BN * kBK];
-  uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
+  using Shape = GemmShape<BN, CTAS>;
+  __nv_bfloat16 a[Shape::kStagesN][kBM * kBK];
+  __nv_bfloat16 b[Shape::kStagesN][Shape::kBNc * kBK];
+  uint64_t full[Shape::kStagesN], empty[Shape::kStagesN], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
-  alignas(128) float4 stage[8][32 * 4]; // per epilogue warp: 32 rows x 16 fp32 columns, 16-byte units swizzled
-                                         // (peer-scatter epilogue: a 32 x 32 bf16 block for one TMA store)
-  float colsum[8][BN / 2]; // per epilogue warp column partials of the GELU-backward epilogue
+  // Per epilogue warp, 4 KB: a 32-row output box for the TMA epilogue (32 fp32
+  // or, in the first 2 KB, 32 bf16 columns; bias+GELU's derivative box in the
+  // second 2 KB); the GELU-backward column partials at byte 2048. The
+  // register-path epilogue stages 32 rows x 16 fp32 columns in the first 2 KB,
+  // the peer scatter a 32 x 32 bf16 block.
+  alignas(1024) uint8_t stage[8][4096];
 };
 
 EB_DEVICE float rcp_approx(float x) {
@@ -224,6 +248,156 @@ EB_DEVICE void epilogue4(const GemmArgs& g, int64_t ooff, int m, int n, float4 v
   }
 }
 
+// Sum over the warp's 32 lanes of each of 32 per-lane values: afterwards lane
+// j holds the sum of everyone's v[j]. Five exchange rounds (16, 8, 4, 2, 1
+// values); in each, a lane keeps the half of its columns selected by its lane
+// bit and adds its partner's copy of that half.
+EB_DEVICE float lane_transpose_sum(float (&v)[32], int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int k = 0; k < s; ++k) {
+      const float send = upper ? v[k] : v[k + s];
+      const float keep = upper ? v[k + s] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+// Byte offset of the 16-byte unit `unit` of row `row` in a swizzled box whose
+// rows are 64 bytes (64-byte swizzle) or 128 bytes (128-byte swizzle) wide;
+// the box starts on a 1024-byte boundary. Eight consecutive rows writing the
+// same unit hit eight different bank groups.
+template <int kRowBytes>
+EB_DEVICE uint32_t swizzled(int row, int unit) {
+  if constexpr (kRowBytes == 64) return row * 64 + ((unit ^ ((row >> 1) & 3)) << 4);
+  else return row * 128 + ((unit ^ (row & 7)) << 4);
+}
+
+// The TMA epilogue of one accumulator tile for one epilogue warp: its 32 rows
+// (lane = row, from TMEM lanes) by its column half, 32 columns per chunk.
+// The chunk's values are finished in registers (bias, GELU, residual, kept
+// derivative), written to the warp's swizzled 32-row box in shared memory and
+// stored (fp32 accumulation: reduced with an element-wise add) by one TMA
+// instruction; the TMA engine clips rows and columns outside the matrix. The
+// box is reused once the previous store has read it. GELU backward also
+// leaves the warp's column sums at byte 2048 of its staging area.
+template <int BN, int EPI>
+EB_DEVICE void tma_epilogue(const GemmArgs& g, const OutMaps& om, uint8_t* stage, uint32_t taddr, int row0,
+                            int col_base, int grp, int lane, int plane) {
+  constexpr bool kF32 = EPI == kStoreF32 || EPI == kAccumF32 || EPI == kBiasResidualF32;
+  const int m = row0 + lane;
+  const bool row_ok = m < g.M;
+  float* colsum = reinterpret_cast<float*>(stage + 2048);
+#pragma unroll 1
+  for (int c0 = grp * (BN / 2); c0 < (grp + 1) * (BN / 2); c0 += 32) {
+    const int n0 = col_base + c0;
+    if (n0 >= g.N) break;                           // uniform across the warp
+    const bool full = n0 + 32 <= g.N;
+    // Per-row operands of the chunk, issued before the TMEM load is awaited.
+    uint4 aux_raw[4];
+    float4 res[8];
+    if constexpr (EPI == kGeluBackBf16) {
+      const __nv_bfloat16* a = g.aux + static_cast<int64_t>(m) * g.ld_aux + n0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        aux_raw[q] = make_uint4(0u, 0u, 0u, 0u);
+        if (row_ok && full) aux_raw[q] = *reinterpret_cast<const uint4*>(a + 8 * q);
+      }
+      if (row_ok && !full) {
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(aux_raw);
+        for (int j = 0; j < 32 && n0 + j < g.N; ++j) e[j] = a[j];
+      }
+    }
+    if constexpr (EPI == kBiasResidualF32) {
+      const float* rrow = g.residual + static_cast<int64_t>(m) * g.ldr + n0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        res[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row_ok && full) res[q] = *reinterpret_cast<const float4*>(rrow + 4 * q);
+      }
+      if (row_ok && !full) {
+        float* e = reinterpret_cast<float*>(res);
+        for (int j = 0; j < 32 && n0 + j < g.N; ++j) e[j] = rrow[j];
+      }
+    }
+    uint32_t r[32];
+    tmem_ld32(taddr + c0, r);
+    tc_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * g.alpha;
+    float kept[32];                                  // bias+GELU: gelu'(pre-activation)
+    if constexpr (EPI == kBiasGeluBf16 || EPI == kBiasResidualF32) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 b4 = g.bias ? load_bias4(g.bias, n0 + 4 * q, g.N) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float& x = v[4 * q + t];
+          if constexpr (EPI == kBiasGeluBf16) {
+            gelu_and_grad(x + bb[t], x, kept[4 * q + t]);
+          } else {
+            const float rr[4] = {res[q].x, res[q].y, res[q].z, res[q].w};
+            x += bb[t] + rr[t];
+          }
+        }
+      }
+    }
+    if constexpr (EPI == kGeluBackBf16) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w[4] = {aux_raw[q].x, aux_raw[q].y, aux_raw[q].z, aux_raw[q].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&w[t]);
+          v[8 * q + 2 * t] *= __low2float(p2);
+          v[8 * q + 2 * t + 1] *= __high2float(p2);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_read_all();             // the previous chunk's stores have read the box
+    __syncwarp();
+    if constexpr (kF32) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<float4*>(stage + swizzled<128>(lane, u)) =
+            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float* x = v + 8 * u;
+        *reinterpret_cast<uint4*>(stage + swizzled<64>(lane, u)) =
+            make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+      }
+      if constexpr (EPI == kBiasGeluBf16) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float* x = kept + 8 * u;
+          *reinterpret_cast<uint4*>(stage + 2048 + swizzled<64>(lane, u)) =
+              make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && row0 < g.M) {
+      if constexpr (EPI == kAccumF32) tma_reduce_add_3d(&om.out, stage, n0, row0, plane);
+      else tma_store_3d(&om.out, stage, n0, row0, plane);
+      if constexpr (EPI == kBiasGeluBf16) tma_store_3d(&om.aux, stage + 2048, n0, row0, 0);
+      bulk_commit();
+    }
+    if constexpr (EPI == kGeluBackBf16) {
+      // Column sums of this chunk over the warp's rows (rows past M hold zeros).
+      const float sum = lane_transpose_sum(v, lane);
+      colsum[c0 - grp * (BN / 2) + lane] = sum;
+    }
+  }
+}
+
 EB_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
   const int per_group = kGroupM * tiles_n;
   const int group = tile / per_group;
@@ -234,36 +408,46 @@ EB_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn)
   tn = in_group / rows;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A, int CTAS>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, GemmArgs g,
-               const __grid_constant__ PeerMaps pm) {
+               const __grid_constant__ PeerMaps pm, const __grid_constant__ OutMaps om) {
+  static_assert(CTAS == 1 || (CTAS == 2 && !GATHER_A && EPI != kScatterBf16), "peer paths run on single CTAs");
+  using Shape = GemmShape<BN, CTAS>;
+  constexpr int kS = Shape::kStagesN;
+  constexpr int kTileM = Shape::kTileM;
+  constexpr int kBNc = Shape::kBNc;
   extern __shared__ __align__(1024) uint8_t raw_smem[];
-  GemmSmem<BN>& sm = *reinterpret_cast<GemmSmem<BN>*>(
+  GemmSmem<BN, CTAS>& sm = *reinterpret_cast<GemmSmem<BN, CTAS>*>(
       (reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
-  constexpr uint32_t kStageBytes = (kBM + BN) * kBK * 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_m = (g.M + kBM - 1) / kBM, tiles_n = (g.N + BN - 1) / BN;
+  const uint32_t rank = CTAS == 2 ? cluster_ctarank() : 0;    // position in the CTA pair
+  const int group = blockIdx.x / CTAS, groups = gridDim.x / CTAS;
+  const int tiles_m = (g.M + kTileM - 1) / kTileM, tiles_n = (g.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
   const int units = tiles * g.splits;     // (split, tile) pairs; consecutive units share a K range
   const int k_blocks = (g.K + kBK - 1) / kBK;
   volatile int* abort = &sm.abort;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 256);
+      mbar_init(&sm.acc_empty[s], 8 * CTAS);   // one arrival per epilogue warp of every CTA of the group
     }
     sm.abort = 0;
     fence_barrier_init();
   }
-  if (warp == 2) tmem_alloc(&sm.tmem_base, kTmemCols);
+  if (warp == 2) {
+    if constexpr (CTAS == 2) tmem_alloc_pair(&sm.tmem_base, kTmemCols);
+    else tmem_alloc(&sm.tmem_base, kTmemCols);
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CTAS == 2) cluster_sync();    // the peer's barriers are initialised before anyone signals them
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
@@ -277,49 +461,70 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       prefetch_tensormap(&tb);
       int it = 0;   // global k-slice counter across tiles
       bool ok = true;
-      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x) {
+      for (int unit = group; ok && unit < units; unit += groups) {
         const int split = unit / tiles, tile = unit - split * tiles;
         int tm, tn;
         tile_coords(tile, tiles_m, tiles_n, tm, tn);
         const int kb0 = split * k_blocks / g.splits, kb1 = (split + 1) * k_blocks / g.splits;
+        const int m0 = tm * kTileM + static_cast<int>(rank) * kBM;     // this CTA's A rows
+        const int n0 = tn * BN + static_cast<int>(rank) * kBNc;        // this CTA's B rows (output columns)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % kStages;
-          if (it >= kStages && !mbar_wait(&sm.empty[s], ((it / kStages) - 1) & 1, abort, g.err, kSiteGemm)) {
+          const int s = it % kS;
+          if (it >= kS && !mbar_wait(&sm.empty[s], ((it / kS) - 1) & 1, abort, g.err, kSiteGemm)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&sm.full[s], kStageBytes);
           const int k0 = kb * kBK;
+          if constexpr (CTAS == 2) {
+            // Both CTAs' bytes complete on the leader's barrier; the leader
+            // arms it for the pair (its arrival is the barrier's only one).
+            const uint32_t bar = cluster_addr(&sm.full[s], 0);
+            if (rank == 0) mbar_expect_tx(&sm.full[s], CTAS * Shape::kStageBytes);
+            if constexpr (A_MN) {
+              tma_load_2d_pair(sm.a[s], &ta, bar, m0, k0);
+              tma_load_2d_pair(sm.a[s] + 64 * kBK, &ta, bar, m0 + 64, k0);
+            } else {
+              tma_load_2d_pair(sm.a[s], &ta, bar, k0, m0);
+            }
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < kBNc / 64; ++j) tma_load_2d_pair(sm.b[s] + j * 64 * kBK, &tb, bar, n0 + 64 * j, k0);
+            } else {
+              tma_load_2d_pair(sm.b[s], &tb, bar, k0, n0);
+            }
+            continue;
+          }
+          mbar_expect_tx(&sm.full[s], Shape::kStageBytes);
           if constexpr (GATHER_A) {
             // A = the sequence layout of rank-sharded head buffers: the 64-wide
             // k-slice lives on one owner; rows are this rank's shard.
             const PeerLayout& L = g.peer;
-            const int m0 = tm * kBM, b = m0 / L.n_local, t0 = m0 - b * L.n_local;
+            const int b = m0 / L.n_local, t0 = m0 - b * L.n_local;
             const int part = k0 / L.dim, within = k0 - part * L.dim;
             const int owner = within / L.C, col = within - owner * L.C;
             tma_load_3d(sm.a[s], &pm.map[owner], &sm.full[s], col, L.rank * L.n_local + t0, part * L.batch + b);
           } else if constexpr (A_MN) {   // A stored [K, M]: boxes of 64 m x 64 k
-            tma_load_2d(sm.a[s], &ta, &sm.full[s], tm * kBM, k0);
-            tma_load_2d(sm.a[s] + 64 * kBK, &ta, &sm.full[s], tm * kBM + 64, k0);
+            tma_load_2d(sm.a[s], &ta, &sm.full[s], m0, k0);
+            tma_load_2d(sm.a[s] + 64 * kBK, &ta, &sm.full[s], m0 + 64, k0);
           } else {                // A stored [M, K]: one box of 64 k x 128 m
-            tma_load_2d(sm.a[s], &ta, &sm.full[s], k0, tm * kBM);
+            tma_load_2d(sm.a[s], &ta, &sm.full[s], k0, m0);
           }
           if constexpr (B_MN) {   // B stored [K, N]: BN/64 boxes of 64 n x 64 k
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sm.b[s] + j * 64 * kBK, &tb, &sm.full[s], tn * BN + 64 * j, k0);
+              tma_load_2d(sm.b[s] + j * 64 * kBK, &tb, &sm.full[s], n0 + 64 * j, k0);
           } else {                // B stored [N, K]: one box of 64 k x BN n
-            tma_load_2d(sm.b[s], &tb, &sm.full[s], k0, tn * BN);
+            tma_load_2d(sm.b[s], &tb, &sm.full[s], k0, n0);
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(kBM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_bf16(kTileM, BN, A_MN, B_MN);
       int it = 0, local = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x, ++local) {
+      for (int unit = group; ok && unit < units; unit += groups, ++local) {
         const int split = unit / tiles;
         const int kb0 = split * k_blocks / g.splits, kb1 = (split + 1) * k_blocks / g.splits;
         const int acc = local & 1;
@@ -327,8 +532,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % kStages;
-          if (!mbar_wait(&sm.full[s], (it / kStages) & 1, abort, g.err, kSiteGemm)) {
+          const int s = it % kS;
+          if (!mbar_wait(&sm.full[s], (it / kS) & 1, abort, g.err, kSiteGemm)) {
             ok = false;
             break;
           }
@@ -340,11 +545,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                                      : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t db = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 64 * kBK * 2, 1024)
                                      : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            mma_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if constexpr (CTAS == 2) mma_ss_pair(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else mma_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&sm.empty[s]);
+          if constexpr (CTAS == 2) {          // the stage is free in both CTAs
+            tc_commit_pair(cluster_addr(&sm.empty[s], 0));
+            tc_commit_pair(cluster_addr(&sm.empty[s], 1));
+          } else {
+            tc_commit(&sm.empty[s]);
+          }
         }
-        if (ok) tc_commit(&sm.acc_full[acc]);
+        if (ok) {
+          if constexpr (CTAS == 2) {
+            tc_commit_pair(cluster_addr(&sm.acc_full[acc], 0));
+            tc_commit_pair(cluster_addr(&sm.acc_full[acc], 1));
+          } else {
+            tc_commit(&sm.acc_full[acc]);
+          }
+        }
       }
     }
   } else if (warp >= 4) {
@@ -356,20 +574,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     const int grp = ew >> 2;                  // column half of the tile
     const int wr = ew & 3;                    // TMEM lane quarter (rows 32*wr..)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(wr * 32) << 16);
-    float4* stage = sm.stage[ew];
+    float4* stage = reinterpret_cast<float4*>(sm.stage[ew]);
+    float* colsum = reinterpret_cast<float*>(sm.stage[ew] + 2048);   // this warp's column partials
     const int rq = lane >> 2, u = lane & 3;
     int local = 0;
-    for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++local) {
+    for (int unit = group; unit < units; unit += groups, ++local) {
       const int split = unit / tiles, tile = unit - split * tiles;
       const int64_t ooff = static_cast<int64_t>(split) * g.split_stride;
       int tm, tn;
       tile_coords(tile, tiles_m, tiles_n, tm, tn);
+      const int row0 = tm * kTileM + static_cast<int>(rank) * kBM;   // this CTA's accumulator rows
       const int acc = local & 1;
       const bool ready = mbar_wait(&sm.acc_full[acc], (local >> 1) & 1, abort, g.err, kSiteGemm);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
+      bool tma_done = false;
+      if constexpr (EPI != kScatterBf16) {
+        if (g.tma_out) {
+          tma_epilogue<BN, EPI>(g, om, sm.stage[ew], lane_addr + acc * BN, row0 + wr * 32, tn * BN, grp, lane,
+                                g.splits > 1 ? split : 0);
+          tma_done = true;
+        }
+      }
 #pragma unroll 1
-      for (int c0 = grp * (BN / 2); c0 < (grp + 1) * (BN / 2); c0 += 32) {
+      for (int c0 = grp * (BN / 2); !tma_done && c0 < (grp + 1) * (BN / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + acc * BN + c0, r);
         if constexpr (EPI == kScatterBf16) {
@@ -395,7 +623,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             __syncwarp();
             if (lane == 0) {
               const PeerLayout& L = g.peer;
-              const int m0 = tm * kBM + wr * 32;
+              const int m0 = row0 + wr * 32;
               const int b = m0 / L.n_local, t0 = m0 - b * L.n_local;
               const int part = n / L.dim, within = n - part * L.dim;
               const int owner = within / L.C, c = within - owner * L.C;
@@ -414,7 +642,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
           for (int it = 0; it < 4; ++it) {
             aux_raw[half][it] = make_uint2(0u, 0u);
             if constexpr (EPI == kGeluBackBf16) {
-              const int m = tm * kBM + wr * 32 + it * 8 + rq;
+              const int m = row0 + wr * 32 + it * 8 + rq;
               const int n = tn * BN + c0 + half * 16 + 4 * u;
               if (g.vec && m < g.M && n + 4 <= g.N)
                 aux_raw[half][it] = *reinterpret_cast<const uint2*>(g.aux + static_cast<int64_t>(m) * g.ld_aux + n);
@@ -442,7 +670,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
           for (int it = 0; it < 4; ++it) {
             const int rr = it * 8 + rq;
             const float4 v = stage[rr * 4 + (u ^ ((rr >> 1) & 3))];
-            const int m = tm * kBM + wr * 32 + rr;
+            const int m = row0 + wr * 32 + rr;
             if (m < g.M && n < g.N) epilogue4<EPI>(g, ooff, m, n, v, bias4, cs, aux_raw[half][it]);
           }
           __syncwarp();
@@ -453,7 +681,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
               for (int o = 4; o < 32; o <<= 1) cs[t] += __shfl_xor_sync(0xffffffffu, cs[t], o);
             }
             if (lane < 4) {
-              float* dst = &sm.colsum[ew][c0 - grp * (BN / 2) + half * 16 + 4 * u];
+              float* dst = &colsum[c0 - grp * (BN / 2) + half * 16 + 4 * u];
               dst[0] = cs[0]; dst[1] = cs[1]; dst[2] = cs[2]; dst[3] = cs[3];
             }
           }
@@ -462,17 +690,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       if constexpr (EPI == kGeluBackBf16) {
         // Combine the group's four row-quarters; one partial row per output tile.
         const int gt = threadIdx.x - 128 - grp * 128;
+        auto part = [&](int w) { return reinterpret_cast<const float*>(sm.stage[w] + 2048); };
         asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
         for (int c = gt; c < BN / 2; c += 128) {
           const int n = tn * BN + grp * (BN / 2) + c;
           if (n < g.N)
-            g.col_partial[static_cast<int64_t>(tm) * g.N + n] = sm.colsum[grp * 4][c] + sm.colsum[grp * 4 + 1][c] +
-                                                               sm.colsum[grp * 4 + 2][c] + sm.colsum[grp * 4 + 3][c];
+            g.col_partial[static_cast<int64_t>(row0 / kBM) * g.N + n] =
+                part(grp * 4)[c] + part(grp * 4 + 1)[c] + part(grp * 4 + 2)[c] + part(grp * 4 + 3)[c];
         }
         asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
       }
+      // The warp's TMEM reads are complete (tcgen05.wait::ld above); one
+      // arrival per warp frees the accumulator (the leader's barrier).
       tc_fence_before();
-      mbar_arrive(&sm.acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CTAS == 2) mbar_arrive_cluster(cluster_addr(&sm.acc_empty[acc], 0));
+        else mbar_arrive(&sm.acc_empty[acc]);
+      }
+    }
+    if constexpr (EPI != kScatterBf16) {
+      if (g.tma_out && lane == 0) bulk_wait_all();   // the epilogue's stores are complete
     }
     // Peer stores complete at system scope before the kernel ends, so a
     // barrier issued after it publishes them.
@@ -482,10 +720,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CTAS == 2) cluster_sync();     // neither CTA leaves while the pair's MMAs may read its memory
+  else __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if constexpr (CTAS == 2) tmem_dealloc_pair(tmem, kTmemCols);
+    else tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -500,27 +740,81 @@ int sm_count(int device) {
   return cached[device];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER_A, int CTAS = 1>
 void launch_gemm(const CUtensorMap& ta, const PeerMaps& pm, const at::Tensor& b, int M, int N, int K,
-                 GemmArgs& args, cudaStream_t stream) {
-  CUtensorMap tb = B_MN ? make_matrix_map(b.data_ptr(), K, N, b.stride(0), kBK)   // [K, N], box 64n x 64k
-                        : make_matrix_map(b.data_ptr(), N, K, b.stride(0), BN);   // [N, K], box 64k x BN n
-  const int units = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * std::max(1, args.splits);
-  const int grid = std::min(units, sm_count(b.device().index()));
-  const size_t smem = sizeof(GemmSmem<BN>) + 1024;
-  auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, EPI, GATHER_A>;
+                 GemmArgs& args, cudaStream_t stream, const OutMaps& om = OutMaps{}) {
+  using Shape = GemmShape<BN, CTAS>;
+  CUtensorMap tb = B_MN ? make_matrix_map(b.data_ptr(), K, N, b.stride(0), kBK)              // [K, N], box 64n x 64k
+                        : make_matrix_map(b.data_ptr(), N, K, b.stride(0), Shape::kBNc);     // [N, K], box 64k x n
+  const int units = ((M + Shape::kTileM - 1) / Shape::kTileM) * ((N + BN - 1) / BN) * std::max(1, args.splits);
+  const size_t smem = sizeof(GemmSmem<BN, CTAS>) + 1024;
+  auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, EPI, GATHER_A, CTAS>;
   EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kernel<<<grid, kThreads, smem, stream>>>(ta, tb, args, pm);
+  const int device = b.device().index();
+  if constexpr (CTAS == 1) {
+    const int grid = std::min(units, sm_count(device));
+    kernel<<<grid, kThreads, smem, stream>>>(ta, tb, args, pm, om);
+  } else {
+    // One CTA pair per pair of SMs that can hold one: as many clusters as fit at once.
+    static int resident[64] = {0};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = CTAS;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const int slot = device >= 0 && device < 64 ? device : 0;
+    if (resident[slot] == 0) {
+      cfg.gridDim = dim3(sm_count(device));
+      int clusters = 0;
+      EB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
+      resident[slot] = std::max(1, clusters);
+    }
+    cfg.gridDim = dim3(CTAS * std::min(units, resident[slot]));
+    EB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, ta, tb, args, pm, om));
+  }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+// Output tile shapes: 128 x 128 and 128 x 256 on one CTA, 256 x 256 on a CTA pair.
+enum TileShape : int { kShapeAuto = 0, kShapeNarrow = 1, kShapeWide = 2, kShapePair = 3 };
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int CTAS = 1>
 void run_gemm(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args, cudaStream_t stream,
               const PeerMaps* pm = nullptr) {
-  // TMA maps: inner (contiguous) dimension first.
+  // TMA maps: inner (contiguous) dimension first. Each CTA stages 128 rows of A.
   CUtensorMap ta = A_MN ? make_matrix_map(a.data_ptr(), K, M, a.stride(0), kBK)     // [K, M], box 64m x 64k
                         : make_matrix_map(a.data_ptr(), M, K, a.stride(0), kBM);    // [M, K], box 64k x 128m
   PeerMaps none{};
-  launch_gemm<BN, A_MN, B_MN, EPI, false>(ta, pm ? *pm : none, b, M, N, K, args, stream);
+  OutMaps om{};
+  if constexpr (EPI != kScatterBf16) {
+    if (args.tma_out) {
+      constexpr bool kF32 = EPI == kStoreF32 || EPI == kAccumF32 || EPI == kBiasResidualF32;
+      const int planes = std::max(1, args.splits);
+      const int64_t plane = planes > 1 ? args.split_stride : static_cast<int64_t>(M) * args.ldo;
+      om.out = make_epilogue_map(args.out, planes, M, N, args.ldo, plane, kF32);
+      if constexpr (EPI == kBiasGeluBf16)
+        om.aux = make_epilogue_map(args.aux, 1, M, N, args.ld_aux, static_cast<int64_t>(M) * args.ld_aux, false);
+    }
+  }
+  launch_gemm<BN, A_MN, B_MN, EPI, false, CTAS>(ta, pm ? *pm : none, b, M, N, K, args, stream, om);
+}
+
+// The TMA epilogue needs 16-byte aligned rows in the output and in the
+// row-wise operands it reads (residual, kept derivative); EB200_GEMM_TMA_EPILOGUE=0
+// selects the register-path epilogue everywhere.
+bool tma_epilogue_ok(const GemmArgs& args, int out_elem) {
+  static const bool off = std::getenv("EB200_GEMM_TMA_EPILOGUE") != nullptr &&
+                          std::string(std::getenv("EB200_GEMM_TMA_EPILOGUE")) == "0";
+  auto ok = [](const void* p, int64_t ld, int elem) {
+    return p == nullptr || ((reinterpret_cast<uintptr_t>(p) % 16) == 0 && (ld * elem) % 16 == 0);
+  };
+  return !off && args.out != nullptr && ok(args.out, args.ldo, out_elem) && ok(args.residual, args.ldr, 4) &&
+         ok(args.aux, args.ld_aux, 2);
 }
 
 bool wide_tiles(int M, int N) {
@@ -529,21 +823,70 @@ bool wide_tiles(int M, int N) {
   return N >= 256 && tiles256 >= 148;
 }
 
-// bn: output tile width, 0 = chosen from the problem size.
+struct GemmPlan {
+  int shape;
+  int splits;
+};
+
+// Tile shape and K split from a small cost model in units of one 128 x 128 x 64
+// MMA step of one SM: waves x (k-blocks per unit x tile width x relative cost
+// per FLOP + the tile's epilogue), plus, when K is split, the partials' round
+// trip through L2 (written once, read once, and the output). Per FLOP a
+// 128-wide tile moves twice the B bytes of a 256-wide one (about 15% slower);
+// a CTA pair stages half of B per SM (about 15% faster than a single CTA).
+// Weight gradients (M, N <= a few thousand, K = tokens) are the shapes that
+// split; token-major GEMMs have enough tiles without it.
+GemmPlan plan_gemm(int M, int N, int K, int sms, bool can_split) {
+  const int k_blocks = (K + kBK - 1) / kBK;
+  constexpr double kStepSeconds = 256.0 / 1.9e9;   // one 128x128x64 step at ~8K FLOP/clock
+  constexpr double kPartialBandwidth = 8e12;        // partials stay in L2 between the two kernels
+  GemmPlan best{N >= 256 ? kShapeWide : kShapeNarrow, 1};
+  double best_t = 1e300;
+  for (int shape : {kShapePair, kShapeWide, kShapeNarrow}) {
+    const int tile_m = shape == kShapePair ? 2 * kBM : kBM;
+    const int bn = shape == kShapeNarrow ? 128 : 256;
+    if (bn == 256 && N < 256) continue;
+    if (shape == kShapePair && M < tile_m) continue;
+    const int slots = shape == kShapePair ? sms / 2 : sms;
+    const double cost = shape == kShapeNarrow ? 1.15 : (shape == kShapePair ? 0.85 : 1.0);
+    const long tiles = static_cast<long>((M + tile_m - 1) / tile_m) * ((N + bn - 1) / bn);
+    const int max_split = can_split ? std::max(1, std::min(16, k_blocks / 4)) : 1;
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const long units = tiles * sp;
+      const long waves = (units + slots - 1) / slots;
+      const double kb = static_cast<double>((k_blocks + sp - 1) / sp);
+      const double unit_t = kb * (bn / 128.0) * cost + 2.0 * bn / 128.0;
+      double t = static_cast<double>(waves) * unit_t;
+      if (sp > 1) t += (sp + 2.0) * M * static_cast<double>(N) * 4.0 / kPartialBandwidth / kStepSeconds;
+      if (t < best_t * 0.97) {
+        best_t = t;
+        best = GemmPlan{shape, sp};
+      }
+    }
+  }
+  return best;
+}
+
+// shape: a TileShape (kShapeAuto = the cost model's choice without a split).
 template <bool A_MN, bool B_MN, int EPI>
 void dispatch_bn(const at::Tensor& a, const at::Tensor& b, int M, int N, int K, GemmArgs& args,
-                 cudaStream_t stream, int bn) {
-  if (bn == 256 || (bn == 0 && wide_tiles(M, N))) run_gemm<256, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
+                 cudaStream_t stream, int shape) {
+  if (shape == kShapeAuto) shape = plan_gemm(M, N, K, sm_count(a.device().index()), false).shape;
+  // A pair tile needs rows for both CTAs; a 256-wide tile needs 256 columns.
+  if (shape == kShapePair && M < 2 * kBM) shape = kShapeWide;
+  if (shape != kShapeNarrow && N < 256) shape = kShapeNarrow;
+  if (shape == kShapePair) run_gemm<256, A_MN, B_MN, EPI, 2>(a, b, M, N, K, args, stream);
+  else if (shape == kShapeWide) run_gemm<256, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
   else run_gemm<128, A_MN, B_MN, EPI>(a, b, M, N, K, args, stream);
 }
 
 template <int EPI>
 void dispatch_layout(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, int M, int N, int K,
-                     GemmArgs& args, cudaStream_t stream, int bn = 0) {
-  if (!a_mn && !b_mn) dispatch_bn<false, false, EPI>(a, b, M, N, K, args, stream, bn);
-  else if (!a_mn && b_mn) dispatch_bn<false, true, EPI>(a, b, M, N, K, args, stream, bn);
-  else if (a_mn && !b_mn) dispatch_bn<true, false, EPI>(a, b, M, N, K, args, stream, bn);
-  else dispatch_bn<true, true, EPI>(a, b, M, N, K, args, stream, bn);
+                     GemmArgs& args, cudaStream_t stream, int shape = kShapeAuto) {
+  if (!a_mn && !b_mn) dispatch_bn<false, false, EPI>(a, b, M, N, K, args, stream, shape);
+  else if (!a_mn && b_mn) dispatch_bn<false, true, EPI>(a, b, M, N, K, args, stream, shape);
+  else if (a_mn && !b_mn) dispatch_bn<true, false, EPI>(a, b, M, N, K, args, stream, shape);
+  else dispatch_bn<true, true, EPI>(a, b, M, N, K, args, stream, shape);
 }
 
 // Sums the split partials ws[0..splits) in split order (so the result does
@@ -572,44 +915,6 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float4* __rest
   }
 }
 
-struct GemmPlan {
-  int bn;
-  int splits;
-};
-
-// Tile width and K split of a GEMM without a fused epilogue, from a small cost
-// model in units of one 128 x 128 x 64 MMA step: waves x (k-blocks per unit x
-// tile width + the tile's epilogue), plus, when K is split, the partials'
-// round trip through L2 (written once, read once, and the output). Narrow
-// tiles run about 15% below wide ones per FLOP (twice the B traffic per FLOP).
-// Weight gradients (M, N <= a few thousand, K = tokens) are the shapes that
-// split; token-major GEMMs have enough tiles without it.
-GemmPlan plan_plain(int M, int N, int K, int sms, bool can_split) {
-  const int k_blocks = (K + kBK - 1) / kBK;
-  constexpr double kStepSeconds = 256.0 / 1.9e9;   // one 128x128x64 step at ~8K FLOP/clock
-  constexpr double kPartialBandwidth = 8e12;        // partials stay in L2 between the two kernels
-  GemmPlan best{N >= 256 ? 256 : 128, 1};
-  double best_t = 1e300;
-  for (int bn : {256, 128}) {
-    if (bn == 256 && N < 256) continue;
-    const long tiles = static_cast<long>((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
-    const int max_split = can_split ? std::max(1, std::min(16, k_blocks / 4)) : 1;
-    for (int sp = 1; sp <= max_split; ++sp) {
-      const long units = tiles * sp;
-      const long waves = (units + sms - 1) / sms;
-      const double kb = static_cast<double>((k_blocks + sp - 1) / sp);
-      const double unit_t = kb * (bn / 128.0) * (bn == 128 ? 1.15 : 1.0) + 2.0 * bn / 128.0;
-      double t = static_cast<double>(waves) * unit_t;
-      if (sp > 1) t += (sp + 2.0) * M * static_cast<double>(N) * 4.0 / kPartialBandwidth / kStepSeconds;
-      if (t < best_t * 0.97) {
-        best_t = t;
-        best = GemmPlan{bn, sp};
-      }
-    }
-  }
-  return best;
-}
-
 bool aligned16(const at::Tensor& t) {
   return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 && (t.stride(0) * 2) % 16 == 0 && t.stride(1) == 1;
 }
@@ -623,9 +928,11 @@ bool gemm_supported(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_
 
 // out = epilogue(alpha * op(A) op(B)^T) where op(A) is [M, K] and op(B) is [N, K].
 // a_mn: A is stored [K, M]; b_mn: B is stored [K, N]. Optional tensors may be undefined.
+// shape: a TileShape to force (tests), 0 = chosen from the problem size.
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t epilogue,
           double alpha, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
-          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial) {
+          const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& col_partial, int64_t shape) {
+  TORCH_CHECK(shape >= kShapeAuto && shape <= kShapePair, "gemm: tile shape 0..3");
   TORCH_CHECK(gemm_supported(a, a_mn, b, b_mn), "gemm: bf16 2-D operands with 16-byte aligned rows required");
   const int M = a_mn ? a.size(1) : a.size(0);
   const int K = a_mn ? a.size(0) : a.size(1);
@@ -660,26 +967,27 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
     args.vec = ok(args.out, args.ldo, out.element_size()) && ok(args.residual, args.ldr, 4) &&
                ok(args.aux, args.ld_aux, 2);
   }
+  args.tma_out = tma_epilogue_ok(args, out.element_size()) ? 1 : 0;
   auto stream = at::cuda::getCurrentCUDAStream();
   switch (epilogue) {
     case kStoreBf16:
       TORCH_CHECK(out.scalar_type() == at::kBFloat16, "bf16 output");
-      dispatch_layout<kStoreBf16>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
+      dispatch_layout<kStoreBf16>(a, a_mn, b, b_mn, M, N, K, args, stream, static_cast<int>(shape)); break;
     case kStoreF32:
       TORCH_CHECK(out.scalar_type() == at::kFloat, "fp32 output");
-      dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
+      dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, static_cast<int>(shape)); break;
     case kAccumF32:
       TORCH_CHECK(out.scalar_type() == at::kFloat, "fp32 output");
-      dispatch_layout<kAccumF32>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
+      dispatch_layout<kAccumF32>(a, a_mn, b, b_mn, M, N, K, args, stream, static_cast<int>(shape)); break;
     case kBiasGeluBf16:
       TORCH_CHECK(out.scalar_type() == at::kBFloat16 && args.aux && args.bias, "bias/aux needed");
-      dispatch_layout<kBiasGeluBf16>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
+      dispatch_layout<kBiasGeluBf16>(a, a_mn, b, b_mn, M, N, K, args, stream, static_cast<int>(shape)); break;
     case kBiasResidualF32:
       TORCH_CHECK(out.scalar_type() == at::kFloat && args.residual, "fp32 residual needed");
-      dispatch_layout<kBiasResidualF32>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
+      dispatch_layout<kBiasResidualF32>(a, a_mn, b, b_mn, M, N, K, args, stream, static_cast<int>(shape)); break;
     case kGeluBackBf16:
       TORCH_CHECK(out.scalar_type() == at::kBFloat16 && args.aux && args.col_partial, "aux/partials needed");
-      dispatch_layout<kGeluBackBf16>(a, a_mn, b, b_mn, M, N, K, args, stream); break;
+      dispatch_layout<kGeluBackBf16>(a, a_mn, b, b_mn, M, N, K, args, stream, static_cast<int>(shape)); break;
     default:
       TORCH_CHECK(false, "unknown epilogue ", epilogue);
   }
@@ -831,7 +1139,8 @@ void gemm_gather(const std::vector<int64_t>& src, int64_t rank, int64_t parts, i
 // no atomics) into the output. `splits`: 0 = chosen by the cost model.
 // Returns the split count used.
 int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, bool accumulate,
-                   int64_t splits) {
+                   int64_t splits, int64_t shape) {
+  TORCH_CHECK(shape >= kShapeAuto && shape <= kShapePair, "gemm_plain: tile shape 0..3");
   TORCH_CHECK(gemm_supported(a, a_mn, b, b_mn), "gemm_plain: bf16 2-D operands with 16-byte aligned rows required");
   const int M = a_mn ? a.size(1) : a.size(0);
   const int K = a_mn ? a.size(0) : a.size(1);
@@ -847,17 +1156,19 @@ int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_m
   // The reduce kernel reads and writes four contiguous elements at a time.
   const bool can_split = out.is_contiguous() && N % 4 == 0 &&
                          reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0 && k_blocks >= 2;
-  GemmPlan plan = plan_plain(M, N, K, sms, can_split);
+  GemmPlan plan = plan_gemm(M, N, K, sms, can_split);
   if (splits > 0) plan.splits = can_split ? static_cast<int>(std::min<int64_t>(splits, k_blocks)) : 1;
+  if (shape != kShapeAuto) plan.shape = static_cast<int>(shape);
   auto stream = at::cuda::getCurrentCUDAStream();
   GemmArgs args = base_args(M, N, K, a);
   args.ldo = out.stride(0);
   if (plan.splits == 1) {
     args.out = out.data_ptr();
     args.vec = (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0 && (args.ldo * out.element_size()) % 16 == 0;
-    if (bf16_out) dispatch_layout<kStoreBf16>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
-    else if (accumulate) dispatch_layout<kAccumF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
-    else dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
+    args.tma_out = tma_epilogue_ok(args, out.element_size()) ? 1 : 0;
+    if (bf16_out) dispatch_layout<kStoreBf16>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.shape);
+    else if (accumulate) dispatch_layout<kAccumF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.shape);
+    else dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.shape);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     count_launch(1);
     return 1;
@@ -868,7 +1179,8 @@ int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_m
   args.splits = plan.splits;
   args.split_stride = static_cast<int64_t>(M) * N;
   args.vec = 1;
-  dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.bn);
+  args.tma_out = tma_epilogue_ok(args, 4) ? 1 : 0;
+  dispatch_layout<kStoreF32>(a, a_mn, b, b_mn, M, N, K, args, stream, plan.shape);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int64_t n4 = static_cast<int64_t>(M) * N / 4;
   const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8));
@@ -883,11 +1195,12 @@ int64_t gemm_plain(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_m
   return plan.splits;
 }
 
-// The plan gemm_plain would use: (tile width, splits), for tests and tools.
+// The plan gemm_plain would use: (tile shape: 1 = 128 x 128, 2 = 128 x 256,
+// 3 = 256 x 256 on a CTA pair; splits), for tests and tools.
 std::vector<int64_t> gemm_plain_plan(int64_t M, int64_t N, int64_t K, int64_t sms) {
-  const GemmPlan plan = plan_plain(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-                                   static_cast<int>(sms), N % 4 == 0 && (K + kBK - 1) / kBK >= 2);
-  return {plan.bn, plan.splits};
+  const GemmPlan plan = plan_gemm(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                  static_cast<int>(sms), N % 4 == 0 && (K + kBK - 1) / kBK >= 2);
+  return {plan.shape, plan.splits};
 }
 
 int64_t gemm_tile_m() { return kBM; }

@@ -25,7 +25,7 @@ precede all G.
 from __future__ import annotations
 
 import math
-import time
+import re
 from numbers import Integral
 
 import torch
@@ -38,7 +38,10 @@ from ..ops import fused
 from ..ops.attention import dense_attention
 from ..parallel.context import ParallelContext
 from ..runtime import trace
-from .blocks import FeedForward, HaloMemoryBlock, KVProjection, RotaryEmbedding, _gather_heads
+from ..data.synthetic import KEY
+from ..ops.gated_reference import block_log_mass, eager_gated
+from ..ops.sparse import TensorPages, sparse_attention
+from .blocks import FeedForward, HaloMemoryBlock, KVProjection, RotaryEmbedding
 
 # On the native path one query tile covers this many supervised positions:
 # the gated-attention kernel never materialises Q x N, so the only memory the
@@ -47,31 +50,36 @@ NATIVE_QUERY_TILE = 65536
 NATIVE_LOSS_TILE = 65536
 
 
+_ARCH_ITEM = re.compile(r"(?P<shared>\((?P<skind>[A-Za-z]+)\)x(?P<scount>\S*))|(?P<kind>[A-Za-z]+)(?:x(?P<count>\S*))?")
+
+
 def parse_arch(arch):
-    """``'Lx2,(G)x4'`` -> ``[(kind, count, shared), ...]`` in application order."""
+    """``'Lx2,(G)x4'`` -> ``[(kind, count, shared), ...]`` in application order.
+
+    ``L`` is a local halo encoder block, ``G`` a global read round; ``XxN``
+    repeats ``X`` N times with independent weights, ``(X)xN`` applies one
+    shared module N times, a bare ``X`` means ``Xx1``; every ``L`` precedes
+    every ``G``.
+    """
     if not isinstance(arch, str) or not arch.strip():
         raise ValueError("arch must be a nonempty spec like 'Lx2,G'")
     spec = []
-    for raw in arch.split(","):
-        item = raw.strip()
-        shared = item.startswith("(")
-        if shared:
-            kind, sep, count = item[1:].partition(")x")
-            if not sep:
+    for item in (part.strip() for part in arch.split(",")):
+        match = _ARCH_ITEM.fullmatch(item)
+        if match is None:
+            if item.startswith("("):
                 raise ValueError(f"shared layers must look like '(X)xN': {item!r}")
-        else:
-            kind, _, count = item.partition("x")
-            count = count or "1"
+            raise ValueError(f"unknown layer kind in arch item {item!r} (want L or G)")
+        shared = match["shared"] is not None
+        kind = match["skind"] if shared else match["kind"]
+        count = match["scount"] if shared else (match["count"] if match["count"] is not None else "1")
         if kind not in ("L", "G"):
             raise ValueError(f"unknown layer kind in arch item {item!r} (want L or G)")
         if not count.isdigit() or int(count) < 1:
             raise ValueError(f"repeat count must be a positive integer in {item!r}")
         spec.append((kind, int(count), shared))
-    kinds = [k for k, _, _ in spec]
-    if "G" in kinds and "L" in kinds:
-        last_l = len(kinds) - 1 - kinds[::-1].index("L")
-        if kinds.index("G") < last_l:
-            raise ValueError("all L layers must precede all G layers (encode -> read)")
+    if "GL" in "".join(kind for kind, _, _ in spec):      # some G before some L
+        raise ValueError("all L layers must precede all G layers (encode -> read)")
     return spec
 
 
@@ -287,7 +295,7 @@ class StackModel(nn.Module):
             x, k, v = self.encode_shard(input_ids, parallel, offset)
         rows = torch.arange(batch, device=device)[:, None]
         native = self._native(x)
-        step = self.pos_chunk or (NATIVE_QUERY_TILE if native else self._chunk_size(n))
+        step = self.pos_chunk or (NATIVE_QUERY_TILE if native else self._reference_chunk(n))
         loss_step = max(self.loss_chunk, NATIVE_LOSS_TILE) if native else self.loss_chunk
         losses, hits = [], []
         for lo in range(0, width, step):
@@ -331,202 +339,116 @@ class StackModel(nn.Module):
             raise ValueError("sup must mark the same positive count per row")
         return sup.nonzero()[:, 1].reshape(sup.shape[0], s), s
 
-    def push_scores(self, q, kb, visible):
-        """Exact block partition functions ``[B,c,H,G]`` (invisible blocks: -inf).
+    # -- whole-sequence forward (inference, validation and the sparse reference) --
 
-        ``q [B,c,H,D]``, ``kb [B,G,b,H,D]``, ``visible [B,c,G]``.
-        """
-        logits = torch.einsum("bchd,bgwhd->bchgw", q, kb) / math.sqrt(self.hd)
-        return logits.logsumexp(-1).masked_fill(~visible[:, :, None, :], float("-inf"))
-
-    def _chunk_size(self, n):
-        """Queries per chunk bounding the sparse-reference temporaries (~2^29-2^31 elements)."""
+    def _reference_chunk(self, n: int) -> int:
+        """Queries per chunk of the materialising top-k read ([chunk, heads, n] logits near 2^27 elements)."""
         if self.pos_chunk > 0:
             return self.pos_chunk
-        groups = -(-n // self.block_size)
-        m = min(self.topk, groups)
-        per_query = self.heads * (n + 2 * m * self.block_size * self.hd)
-        small = self.dim <= 512
-        cap, budget = (2048, 1 << 31) if small else (512, 1 << 29)
-        return min(cap, max(16, budget // max(per_query, 1)))
+        return max(16, min(4096, (1 << 27) // max(1, 3 * self.heads * n)))
 
-    def _read_round_sparse(self, rd, z, sl, env):
-        """Differentiable top-k read round (mathematical reference, any grad mode)."""
-        batch, count, _ = z.shape
-        n, b, groups = env["n"], env["b"], env["groups"]
-        pos = env["pos"][:, sl]
-        window = env["src"][:, sl]                                   # [B,c,2b]
-        rows3 = env["rows3"]
-        k_local = env["raw_k"][rows3, window.clamp(0, n - 1)]        # [B,c,2b,H,D]
-        v_local = env["raw_v"][rows3, window.clamp(0, n - 1)]
-        q = rd.wq(rd.q_norm(z)).reshape(batch, count, self.heads, self.hd)
-        s = self.push_scores(q, env["kb"], env["visible"][:, sl])    # [B,c,H,G]
-        with torch.no_grad():
-            top, sel = s.topk(min(self.topk, groups), dim=-1)
-            sel_ok = torch.isfinite(top)
-        gate = torch.nan_to_num(s - s.logsumexp(-1, keepdim=True), nan=0.0, neginf=0.0)
-        gate_sel = torch.where(sel_ok, gate.gather(3, sel), torch.zeros((), dtype=gate.dtype,
-                                                                       device=gate.device))
-        tokens = (sel[..., None] * b + torch.arange(b, device=z.device)).reshape(
-            batch, count, self.heads, -1)                            # [B,c,H,m*b]
-        tok_ok = (sel_ok[..., None].expand(-1, -1, -1, -1, b).reshape(batch, count, self.heads, -1)
-                  & (tokens < n) & (tokens <= pos[:, :, None, None]))
-        idx = tokens.clamp(0, n - 1).permute(0, 2, 1, 3)
-        k_remote = _gather_heads(env["raw_k"].transpose(1, 2), idx).permute(0, 2, 1, 3, 4)
-        v_remote = _gather_heads(env["raw_v"].transpose(1, 2), idx).permute(0, 2, 1, 3, 4)
-        bias = gate_sel[..., None].expand(-1, -1, -1, -1, b).reshape(batch, count, self.heads, -1)
-        s_local = torch.einsum("bchd,bcwhd->bchw", q, k_local) / math.sqrt(self.hd)
-        s_remote = torch.einsum("bchd,bchkd->bchk", q, k_remote) / math.sqrt(self.hd) + bias
-        mask = torch.cat([env["src_valid"][:, sl, None].expand(-1, -1, self.heads, -1), tok_ok], -1)
-        probs = torch.cat([s_local, s_remote], -1).masked_fill(~mask, float("-inf")).softmax(-1)
-        width = s_local.shape[-1]
-        ctx = (torch.einsum("bchw,bcwhd->bchd", probs[..., :width], v_local)
-               + torch.einsum("bchk,bchkd->bchd", probs[..., width:], v_remote))
-        z = z + rd.read_out(ctx.reshape(batch, count, self.dim))
-        return z + rd.ffn(rd.ffn_norm(z))
+    def _read(self, rd, z, raw_k, raw_v, positions, blocks):
+        """One G round for the states ``z`` of ``positions`` over an unsharded sequence.
 
-    def _prof_tick(self, device):
-        """Phase timer (enable with ``model._prof = True``); synchronises the device."""
-        if not getattr(self, "_prof", False):
-            return None
-        if device.type == "cuda":
-            torch.cuda.synchronize(device)
-        return time.perf_counter()
+        With ``topk`` at least the number of blocks every block is read: the
+        dense gated operator (native kernels on CUDA). Otherwise the top-k rule
+        applies: without autograd through the paged sparse operator, with
+        autograd through the materialising reference (its gate is
+        differentiable, unselected blocks included).
+        """
+        if self.topk >= blocks:
+            return self._dense_round(rd, z, raw_k, raw_v, positions, ParallelContext())
+        q = self._query(rd, z).view(*z.shape[:2], self.heads, self.hd)
+        if torch.is_grad_enabled():
+            ctx = eager_gated(q, raw_k, raw_v, positions, self.block_size, topk=self.topk)
+        else:
+            pages = TensorPages(raw_k, raw_v, page_tokens=max(self.block_size, 65536 // self.block_size * self.block_size))
+            ctx = sparse_attention(q, pages, positions, self.block_size, self.topk, self.backend)
+        return self._finish(rd, z, ctx.reshape(*z.shape[:2], self.dim))
+
+    def _positions(self, sup, batch, n, device):
+        pos, count = self.supervised_positions(sup, n)
+        if pos is None:
+            pos = torch.arange(n, device=device)[None].expand(batch, n)
+        return pos.to(device), count
+
+    @staticmethod
+    def _rows(x, positions):
+        return torch.gather(x, 1, positions[..., None].expand(-1, -1, x.shape[-1]))
 
     def forward(self, input_ids, sup=None, *, targets=None, parallel=None, offset=0, compact=False):
+        """Logits ``[B, N, V]`` (zero off ``sup``), or ``[B, S, V]`` at the supervised positions
+        with ``compact``; with ``targets`` the training loss sums of :meth:`forward_loss`."""
         if targets is not None:
             return self.forward_loss(input_ids, targets, sup, parallel, offset)
-        if input_ids.ndim != 2 or min(input_ids.shape) < 1:
-            raise ValueError("input_ids must have nonempty shape [batch, sequence]")
-        batch, n = input_ids.shape
-        b = self.block_size
-        groups = -(-n // b)
-        t0 = self._prof_tick(input_ids.device)
-        x, raw_k, raw_v = self.encode(input_ids)
-        t1 = self._prof_tick(input_ids.device)
-        pos, s_n = self.supervised_positions(sup, n)
-        if pos is None:
-            pos = torch.arange(n, device=x.device)[None].expand(batch, n)
-        dense = self.topk >= groups
-        sparse_grad = not dense and torch.is_grad_enabled()
-        env = None
-        if sparse_grad:
-            kb = F.pad(raw_k, (0, 0, 0, 0, 0, groups * b - n)).reshape(batch, groups, b, self.heads,
-                                                                       self.hd)
-            block_end = (torch.arange(groups, device=x.device) + 1) * b
-            env = dict(n=n, b=b, groups=groups, kb=kb, raw_k=raw_k, raw_v=raw_v,
-                       rows3=torch.arange(batch, device=x.device)[:, None, None])
-        rows = torch.arange(batch, device=x.device)[:, None]
-        window = torch.arange(2 * b, device=x.device)
-        outs = []
-        chunk = self._chunk_size(n)
-        for start in range(0, s_n, chunk):
-            sl = slice(start, min(s_n, start + chunk))
-            pc = pos[:, sl]
-            z = x[rows, pc]
-            if sparse_grad:
-                block_of = torch.div(pc, b, rounding_mode="floor")
-                first_valid = ((block_of - 1) * b).clamp_min(0)
-                src = pc[:, :, None] - (2 * b - 1) + window
-                env.update(pos=pc, src=src,
-                           src_valid=(src >= first_valid[:, :, None]) & (src >= 0),
-                           visible=block_end[None, None, :] <= ((block_of - 1) * b)[:, :, None])
-            for rd in self.reads:
-                if dense:
-                    z = self._dense_round(rd, z, raw_k, raw_v, pc, ParallelContext())
-                elif not torch.is_grad_enabled():
-                    from ..ops.sparse import TensorPages, sparse_attention
-                    q = self._query(rd, z).reshape(batch, z.shape[1], self.heads, self.hd)
-                    pages = TensorPages(raw_k, raw_v, page_tokens=max(b, 65536 // b * b))
-                    ctx = sparse_attention(q, pages, pc, b, min(self.topk, groups), self.backend)
-                    z = self._finish(rd, z, ctx.reshape(batch, z.shape[1], self.dim))
-                else:
-                    z = self._read_round_sparse(rd, z, slice(None), env)
-            outs.append(z)
-        t2 = self._prof_tick(input_ids.device)
-        z = outs[0] if len(outs) == 1 else torch.cat(outs, dim=1)
-        sup_logits = fused.linear(fused.layer_norm(z, self.final_norm, self.backend), self.lm_head,
-                                  self.backend)
+        batch, n = input_ids.shape if input_ids.ndim == 2 else (0, 0)
+        with trace.phase("encode"):
+            x, raw_k, raw_v = self.encode(input_ids)
+        pos, count = self._positions(sup, batch, n, x.device)
+        blocks = -(-n // self.block_size)
+        step = self._reference_chunk(n)
+        states = []
+        with trace.phase("read_rounds"):
+            for lo in range(0, count, step):
+                part = pos[:, lo:lo + step]
+                z = self._rows(x, part)
+                for rd in self.reads:
+                    z = self._read(rd, z, raw_k, raw_v, part, blocks)
+                states.append(z)
+        z = states[0] if len(states) == 1 else torch.cat(states, 1)
+        picked = fused.linear(fused.layer_norm(z, self.final_norm, self.backend), self.lm_head, self.backend)
         if compact:
-            return sup_logits
-        logits = sup_logits.new_zeros(batch, n, sup_logits.shape[-1])
-        logits[rows, pos] = sup_logits
-        t3 = self._prof_tick(input_ids.device)
-        if t0 is not None:
-            self._prof_stats = {"enc_s": round(t1 - t0, 3), "read_s": round(t2 - t1, 3),
-                                "head_s": round(t3 - t2, 3)}
-        return logits
+            return picked
+        logits = picked.new_zeros(batch, n, picked.shape[-1])
+        return logits.scatter(1, pos[..., None].expand(-1, -1, picked.shape[-1]), picked)
 
     @torch.no_grad()
     def diagnose(self, idx, sup=None, needle_pos=None):
-        """Selection quality of the first G round (push only, no pop).
+        """How well the first G round's top-k captures its gate, from block scores alone.
 
-        ``sel_cov``: attention mass covered by the selected blocks;
-        ``gate_margin``: lowest selected minus highest unselected visible score;
-        ``needle_block_hit`` (passkey): fraction of heads whose top-k holds a
-        needle block at the first supervised position, over rows whose needle
-        lies outside the local window (reference: st/models/stack.py:463-534).
+        * ``sel_cov``: softmax mass (over remote block scores) of the kept blocks;
+        * ``gate_margin``: weakest kept minus strongest dropped remote block score;
+        * ``needle_block_hit`` (passkey, ``needle_pos [B]``): at each row's first
+          supervised position, the fraction of heads that keep a block of the
+          needle, over rows whose needle lies before the local window.
         """
         if not self.reads:
             return {}
         self.eval()
         batch, n = idx.shape
         b = self.block_size
-        groups = -(-n // b)
         x, raw_k, _ = self.encode(idx)
-        pos, s_n = self.supervised_positions(sup, n)
-        if pos is None:
-            pos = torch.arange(n, device=x.device)[None].expand(batch, n)
-        block_of = torch.div(pos, b, rounding_mode="floor")
-        kb = F.pad(raw_k, (0, 0, 0, 0, 0, groups * b - n)).reshape(batch, groups, b, self.heads,
-                                                                   self.hd)
-        block_end = (torch.arange(groups, device=x.device) + 1) * b
+        pos, count = self._positions(sup, batch, n, x.device)
         rd = self.reads[0]
-        rows = torch.arange(batch, device=x.device)[:, None]
-        keep = min(self.topk, groups)
-        cov = [0.0, 0.0]
-        margin = [0.0, 0.0]
-        needle = [0.0, 0.0]
-        step = self._chunk_size(n)
-        for start in range(0, s_n, step):
-            stop = min(s_n, start + step)
-            count = stop - start
-            visible = block_end[None, None, :] <= ((block_of[:, start:stop] - 1) * b)[:, :, None]
-            z = x[rows, pos[:, start:stop]]
-            q = rd.wq(rd.q_norm(z)).reshape(batch, count, self.heads, self.hd)
-            s = self.push_scores(q, kb, visible)
-            top, sel = s.topk(keep, dim=-1)
-            sel_ok = torch.isfinite(top)
-            p = s.softmax(-1)
-            p_sel = torch.where(sel_ok, p.gather(3, sel), torch.zeros((), dtype=p.dtype,
-                                                                      device=p.device))
-            coverage = p_sel.sum(-1)
-            has_visible = visible.any(-1, keepdim=True).expand_as(coverage)
-            cov[0] += coverage[has_visible].sum().item()
-            cov[1] += has_visible.sum().item()
-            chosen = torch.zeros_like(s, dtype=torch.bool).scatter(3, sel, sel_ok)
-            unchosen = visible[:, :, None, :] & ~chosen
-            lowest = s.masked_fill(~chosen, float("inf")).min(-1).values
-            highest = s.masked_fill(~unchosen, float("-inf")).max(-1).values
-            both = chosen.any(-1) & unchosen.any(-1)
-            margin[0] += (lowest - highest)[both].sum().item()
-            margin[1] += both.sum().item()
-            if needle_pos is not None and start == 0:
-                needle_blocks = torch.div(needle_pos.to(x.device)[:, None]
-                                          + torch.arange(6, device=x.device), b,
-                                          rounding_mode="floor")
-                first_block = int(pos[0, 0]) // b
-                outside = needle_blocks.max(-1).values <= first_block - 2
-                if outside.any():
-                    at_first = chosen[:, 0]
-                    hit = at_first.gather(2, needle_blocks[:, None, :].expand(-1, self.heads, -1)).any(-1)
-                    needle[0] += hit[outside].float().mean(-1).sum().item()
-                    needle[1] += int(outside.sum().item())
-        out = {}
-        if cov[1]:
-            out["sel_cov"] = round(cov[0] / cov[1], 4)
-        if margin[1]:
-            out["gate_margin"] = round(margin[0] / margin[1], 4)
-        if needle[1]:
-            out["needle_block_hit"] = round(needle[0] / needle[1], 4)
-        return out
+        sums = torch.zeros(6, dtype=torch.float64, device=x.device)   # coverage, margin, needle: (sum, count)
+        step = self._reference_chunk(n)
+        for lo in range(0, count, step):
+            part = pos[:, lo:lo + step]
+            q = self._query(rd, self._rows(x, part)).view(batch, part.shape[1], self.heads, self.hd)
+            scores = block_log_mass(q, raw_k, part, b)                # [B,c,H,G]
+            remote = torch.isfinite(scores)
+            top, chosen = scores.topk(min(self.topk, scores.shape[-1]), -1)
+            kept = torch.zeros_like(remote).scatter(-1, chosen, torch.isfinite(top))
+            dropped = remote & ~kept
+            any_remote = remote.any(-1)
+            share = torch.where(kept, scores.softmax(-1), torch.zeros_like(scores)).sum(-1)
+            sums[0] += share[any_remote].sum()
+            sums[1] += any_remote.sum()
+            both = kept.any(-1) & dropped.any(-1)
+            gap = scores.masked_fill(~kept, math.inf).amin(-1) - scores.masked_fill(~dropped, -math.inf).amax(-1)
+            sums[2] += gap[both].sum()
+            sums[3] += both.sum()
+            if needle_pos is not None and lo == 0:
+                width = KEY + 1                                        # the needle: marker and key digits
+                needle_blocks = (needle_pos.to(x.device)[:, None] + torch.arange(width, device=x.device)) // b
+                before_window = needle_blocks.amax(-1) <= part[:, 0] // b - 2
+                hit = kept[:, 0].gather(-1, needle_blocks[:, None, :].expand(-1, self.heads, -1)).any(-1)
+                sums[4] += hit.double().mean(-1)[before_window].sum()
+                sums[5] += before_window.sum()
+        totals = sums.tolist()
+        report = {}
+        for name, (total, n_items) in zip(("sel_cov", "gate_margin", "needle_block_hit"),
+                                          zip(totals[0::2], totals[1::2])):
+            if n_items:
+                report[name] = round(total / n_items, 4)
+        return report

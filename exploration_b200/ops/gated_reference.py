@@ -186,24 +186,54 @@ def gated_backward(grad, q, k, v, positions, out, remote_ctx, remote_prob, log_z
     return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
 
 
-def eager_gated(q, k, v, positions, block_size):
-    """Materialising ``Q x N`` form of the same operator (for small checks)."""
+def _logits(q, k):
+    """``a = q . k / sqrt(D)`` as ``[B, H, Q, N]`` in the work dtype."""
+    dtype = work_dtype(q)
+    return (q.transpose(1, 2).to(dtype) @ k.transpose(1, 2).to(dtype).transpose(-1, -2)) / math.sqrt(q.shape[-1])
+
+
+def _visible_block_scores(a, positions, b):
+    """Block scores ``s_j = logsumexp_{i in j} a_i`` ``[B, H, Q, G]``, ``-inf`` off the remote blocks
+    (blocks ``j < P - 1`` of a query in block ``P``), and the visibility mask."""
+    n = a.shape[-1]
+    s = torch.nn.functional.pad(a, (0, (-n) % b), value=NEG_INF).unflatten(-1, (-1, b)).logsumexp(-1)
+    blocks = torch.arange(s.shape[-1], device=a.device)
+    visible = blocks < torch.div(positions[:, None, :, None], b, rounding_mode="floor") - 1
+    return s.masked_fill(~visible, NEG_INF), visible
+
+
+def block_log_mass(q, k, positions, block_size):
+    """Remote block scores ``[B, Q, H, G]`` of queries ``q [B, Q, H, D]`` at ``positions [B, Q]``
+    over keys ``k [B, N, H, D]`` (``-inf`` for blocks that are not remote to the query)."""
+    s, _ = _visible_block_scores(_logits(q, k), positions, block_size)
+    return s.transpose(1, 2)
+
+
+def eager_gated(q, k, v, positions, block_size, topk=None):
+    """Materialising ``Q x N`` form of the operator (small checks and the differentiable top-k read).
+
+    With ``topk``, a query reads remote keys only from its ``topk`` highest
+    scoring remote blocks per head (the inference rule); the gate still
+    normalises over every remote block, so unselected blocks receive gradient
+    through ``log Z_R``. ``topk=None`` (or at least the number of blocks) is
+    the dense training operator.
+    """
     b = block_size
     n = k.shape[1]
-    dtype = work_dtype(q)
-    a = (q.transpose(1, 2).to(dtype) @ k.transpose(1, 2).to(dtype).transpose(-1, -2)) \
-        / math.sqrt(q.shape[-1])
-    padded = torch.nn.functional.pad(a, (0, (-n) % b), value=NEG_INF)
-    s = padded.unflatten(-1, (-1, b)).logsumexp(-1)
-    blocks = torch.arange(s.shape[-1], device=q.device)
-    pos = positions[:, None, :, None]
-    visible = blocks[None, None, None, :] < torch.div(pos, b, rounding_mode="floor") - 1
-    s = s.masked_fill(~visible, NEG_INF)
+    a = _logits(q, k)                                                  # [B,H,Q,N]
+    s, visible = _visible_block_scores(a, positions, b)
     any_remote = visible.any(-1, keepdim=True)
     safe = torch.where(any_remote, s, torch.zeros_like(s))
     gate = (safe - safe.logsumexp(-1, keepdim=True)).masked_fill(~visible, 0.0)
-    bias = gate.repeat_interleave(b, -1)[..., :n]
-    causal = torch.arange(n, device=q.device)[None, None, None, :] <= pos
-    probs = (a + bias).masked_fill(~causal, NEG_INF).softmax(-1)
-    probs = torch.nan_to_num(probs, nan=0.0)
-    return (probs @ v.transpose(1, 2).to(dtype)).transpose(1, 2).to(q.dtype)
+    read = visible
+    if topk is not None and topk < s.shape[-1]:
+        with torch.no_grad():
+            top, chosen = s.topk(topk, -1)
+            read = torch.zeros_like(s, dtype=torch.bool).scatter(-1, chosen, torch.isfinite(top))
+    key_block = torch.arange(n, device=q.device) // b
+    pos = positions[:, None, :, None]
+    local = key_block >= torch.div(pos, b, rounding_mode="floor") - 1
+    allowed = (torch.arange(n, device=q.device) <= pos) & (local | read[..., key_block])
+    bias = gate[..., key_block]
+    probs = torch.nan_to_num((a + bias).masked_fill(~allowed, NEG_INF).softmax(-1), nan=0.0)
+    return (probs @ v.transpose(1, 2).to(a.dtype)).transpose(1, 2).to(q.dtype)

@@ -43,17 +43,22 @@ def supported(*tensors) -> bool:
     return all(t.is_cuda and _aligned(t) for t in tensors)
 
 
-def gemm(a, a_mn, b, b_mn, out, epilogue, alpha=1.0, bias=None, residual=None, aux=None, partial=None):
+# Tile shapes of the kernel (``shape=`` forces one; 0 lets the cost model choose).
+AUTO, NARROW, WIDE, PAIR = range(4)      # -, 128 x 128, 128 x 256, 256 x 256 on a CTA pair
+
+
+def gemm(a, a_mn, b, b_mn, out, epilogue, alpha=1.0, bias=None, residual=None, aux=None, partial=None,
+         shape=AUTO):
     ext = _native.native(a)
-    ext.gemm(a, a_mn, b, b_mn, out, epilogue, alpha, bias, residual, aux, partial)
+    ext.gemm(a, a_mn, b, b_mn, out, epilogue, alpha, bias, residual, aux, partial, shape)
     record("gemm_tc", epilogue=epilogue, a_mn=a_mn, b_mn=b_mn)
     return out
 
 
-def plain(a, a_mn, b, b_mn, out, accumulate=False, splits=0):
+def plain(a, a_mn, b, b_mn, out, accumulate=False, splits=0, shape=AUTO):
     """``out (+)= op(A) op(B)^T`` with no epilogue (split-K when the output has few tiles)."""
     ext = _native.native(a)
-    used = ext.gemm_plain(a, a_mn, b, b_mn, out, accumulate, splits)
+    used = ext.gemm_plain(a, a_mn, b, b_mn, out, accumulate, splits, shape)
     record("gemm_tc", epilogue="accumulate" if accumulate else "store", a_mn=a_mn, b_mn=b_mn, splits=used)
     return out
 

@@ -277,61 +277,71 @@ def train(args, model, parallel, ck, dataset, validation_dataset=None):
         trainer.close()
 
 
+def _query_positions(args, mask):
+    """``[B, S]`` absolute positions whose next token is scored."""
+    if args.eval_positions:
+        # A fixed, evenly spread set that always includes the last position.
+        width = min(args.eval_positions, args.length)
+        return torch.linspace(0, args.length - 1, width).round().long()[None].expand(args.batch_size, -1)
+    counts = mask.sum(1)
+    if int(counts.max()) != int(counts.min()) or int(counts.min()) == 0:
+        raise ValueError("inference task masks must have equal nonzero counts per row")
+    return mask.nonzero()[:, 1].view(args.batch_size, -1)
+
+
+@contextlib.contextmanager
+def _logit_stream(args, model, parallel, ids, positions, first: bool):
+    """Yields an iterator of ``(slice, logits)`` over ``positions``.
+
+    Stack models run the paged sparse session (prefill into the tiered K/V
+    cache, then the read rounds chunk by chunk); the dense baseline encodes
+    once and projects the requested positions slice by slice.
+    """
+    if not isinstance(model, StackModel):
+        device = next(model.parameters()).device
+        yield ((sl, logits) for sl, logits, _ in model.iter_logits(ids.to(device), positions.to(device),
+                                                                    parallel=parallel))
+        return
+    group = dist.group.WORLD if parallel.world_size > 1 else None
+    with InferenceSession(model, group=group, cache=args.cache, cache_dir=args.cache_dir or None,
+                          memory_fraction=args.memory_fraction, page_tokens=args.page_tokens,
+                          encoder_chunk=args.encoder_chunk, query_chunk=args.inference_query_chunk,
+                          workspace_mb=args.workspace_mb, max_query_states_mb=args.max_query_states_mb) as session:
+        session.prefill(ids, positions)
+        if first:
+            emit({"event": "inference_plan", "batch": 0, **session.plan.to_dict()}, args, parallel.rank)
+        yield ((sl, logits) for sl, logits, _ in session.iter_logits())
+
+
 @torch.no_grad()
 def evaluate(args, model, parallel, dataset, during_training=False, step=None):
+    """Score ``eval_batches`` batches; token metrics and exact match stay on the device until the end."""
     model.eval()
     if args.precision == "bf16" and not during_training:
         model.to(torch.bfloat16)
-    group = dist.group.WORLD if parallel.world_size > 1 else None
-    generator = torch.Generator().manual_seed(args.seed + 200)
-    metrics = MetricAccumulator(parse_bucket_edges(getattr(args, "metric_buckets", "auto"), args.length))
-    metrics.start_rows(0, track_rows=False)
-    exact = rows = 0
-    begin = time.perf_counter()
     on_gpu = next(model.parameters()).is_cuda
     if on_gpu and not during_training:
         torch.cuda.reset_peak_memory_stats()
-    for batch_index in range(args.eval_batches):
+    generator = torch.Generator().manual_seed(args.seed + 200)
+    metrics = MetricAccumulator(parse_bucket_edges(getattr(args, "metric_buckets", "auto"), args.length))
+    metrics.start_rows(0, track_rows=False)
+    exact_rows = None
+    begin = time.perf_counter()
+    for index in range(args.eval_batches):
         ids, targets, mask, _ = make_batch(args, generator, dataset)
-        if args.eval_positions:
-            width = min(args.eval_positions, args.length)
-            positions = torch.linspace(0, args.length - 1, width).round().long()[None].expand(
-                args.batch_size, -1)
-        else:
-            counts = mask.sum(1)
-            if int(counts.max()) != int(counts.min()) or int(counts.min()) == 0:
-                raise ValueError("inference task masks must have equal nonzero counts per row")
-            positions = mask.nonzero()[:, 1].reshape(args.batch_size, -1)
+        positions = _query_positions(args, mask)
         truth = targets.gather(1, positions)
-        errors = torch.zeros(args.batch_size, dtype=torch.long)
-        if isinstance(model, StackModel):
-            session = InferenceSession(model, group=group, cache=args.cache,
-                                       cache_dir=args.cache_dir or None,
-                                       memory_fraction=args.memory_fraction,
-                                       page_tokens=args.page_tokens, encoder_chunk=args.encoder_chunk,
-                                       query_chunk=args.inference_query_chunk,
-                                       workspace_mb=args.workspace_mb,
-                                       max_query_states_mb=args.max_query_states_mb)
-        else:
-            session = contextlib.nullcontext()
-        with session as active:
-            if active is not None:
-                active.prefill(ids, positions)
-                if batch_index == 0:
-                    emit({"event": "inference_plan", "batch": batch_index, **active.plan.to_dict()},
-                         args, parallel.rank)
-                chunks = active.iter_logits()
-            else:
-                device = next(model.parameters()).device
-                chunks = model.iter_logits(ids.to(device), positions.to(device), parallel=parallel)
-            for sl, logits, _ in chunks:
+        wrong = None
+        with _logit_stream(args, model, parallel, ids, positions, index == 0) as stream:
+            for sl, logits in stream:
                 target = truth[:, sl].to(logits.device)
-                errors += (~logits.argmax(-1).eq(target)).sum(1).cpu()
                 metrics.update(logits, target, positions[:, sl].to(logits.device))
-        exact += int((errors == 0).sum())
-        rows += args.batch_size
+                misses = (logits.argmax(-1) != target).sum(1)
+                wrong = misses if wrong is None else wrong + misses
+        solved = (wrong == 0).sum()
+        exact_rows = solved if exact_rows is None else exact_rows + solved
     summary = metrics.finalize()
-    summary["exact"] = exact / max(1, rows)
+    summary["exact"] = int(exact_rows) / max(1, args.eval_batches * args.batch_size)
     result = {"event": "eval", **({"step": step} if step is not None else {}), "length": args.length,
               **{k: round(v, 6) if isinstance(v, float) else v for k, v in summary.items()},
               "seconds": round(time.perf_counter() - begin, 3),
@@ -343,96 +353,119 @@ def evaluate(args, model, parallel, dataset, during_training=False, step=None):
     return result
 
 
-def run(args):
-    torch.manual_seed(args.seed)
-    random.seed(args.seed)
-    ck = ckpt.load(args.resume) if args.resume else None
+# ---------------------------------------------------------------------------
+# the commands
+# ---------------------------------------------------------------------------
+
+def _resolve_architecture(args, ck) -> dict:
+    """Model options from the checkpoint (resume) or the flags, written back onto ``args``."""
     if args.task == "enwik8":
-        args.vocab_size = 256
+        args.vocab_size = 256                      # byte tokens
     options = dict(ckpt.model_config(ck)) if ck is not None else model_options(args)
     options.setdefault("model", "stack")
     if args.topk is not None and options["model"] == "stack":
-        options["topk"] = args.topk
+        options["topk"] = args.topk                # inference-time override of the read width
     for key, value in options.items():
         setattr(args, key, value)
     args.topk = options.get("topk", 64)
-    execution = ExecutionConfig(backend=args.backend, checkpoint_chunks=args.checkpoint_chunks,
-                                encoder_chunk=args.encoder_chunk, query_chunk=args.query_chunk,
-                                loss_chunk=args.loss_chunk, flash_attention=args.flash_attention,
-                                attention_q_chunk=args.attention_q_chunk,
-                                attention_kv_chunk=args.attention_kv_chunk)
-    model = build_model(options, device="meta" if args.command == "plan" else "cpu", execution=execution)
+    return options
+
+
+def _execution(args) -> ExecutionConfig:
+    return ExecutionConfig(backend=args.backend, checkpoint_chunks=args.checkpoint_chunks,
+                           encoder_chunk=args.encoder_chunk, query_chunk=args.query_chunk,
+                           loss_chunk=args.loss_chunk, flash_attention=args.flash_attention,
+                           attention_q_chunk=args.attention_q_chunk, attention_kv_chunk=args.attention_kv_chunk)
+
+
+def _plan_report(args, model, options) -> None:
+    kv_element = 2 if args.precision == "bf16" else 4
+    report = {"model": options,
+              "training": [training_estimate(model, args.batch_size, args.length, c, args.checkpoint_chunks)
+                           for c in (1, 2, 4, 8) if model.heads % c == 0],
+              "inference_raw_kv_bytes": (2 * args.batch_size * args.length * model.dim * kv_element
+                                         if isinstance(model, StackModel) else None)}
+    print(json.dumps(report, indent=2))
+
+
+def _this_rank_device(args):
+    """``(device, HBM capacity)`` of this process (CPU runs get a nominal 64 GiB)."""
+    if args.device != "cuda":
+        return torch.device("cpu"), 64 * GiB
+    if not torch.cuda.is_available():
+        raise RuntimeError("NVIDIA CUDA is required; use --device cpu for the reference path")
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    device = torch.device("cuda", torch.cuda.current_device())
+    return device, torch.cuda.mem_get_info(device)[1]
+
+
+def _datasets(args):
+    """``(data, validation data)``; ``None`` for the synthetic tasks."""
+    if args.task == "tokens":
+        validation = TokenDataset(args.validation_tokens, args.token_dtype) if args.validation_tokens else None
+        return TokenDataset(args.tokens, args.token_dtype), validation
+    if args.task == "enwik8":
+        path = args.tokens or "data/enwik8"
+        training = args.command == "train"
+        validation = enwik8_dataset(path, args.split) if training and args.eval_every else None
+        return enwik8_dataset(path, "train" if training else args.split), validation
+    return None, None
+
+
+def run(args):
+    """``plan``, ``train`` or ``eval`` for one process of a (torchrun) job of 1..8 ranks."""
+    torch.manual_seed(args.seed)
+    random.seed(args.seed)
+    ck = ckpt.load(args.resume) if args.resume else None
+    options = _resolve_architecture(args, ck)
+    model = build_model(options, device="meta" if args.command == "plan" else "cpu", execution=_execution(args))
     if ck is not None:
+        state = ck.pop("model")
         if args.command != "plan":
-            model.load_state_dict(ck["model"], strict=True)
-        ck.pop("model")
+            model.load_state_dict(state, strict=True)
         if args.command != "train":
-            ck.clear()
+            ck.clear()                             # only training resumes optimizer and RNG state
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if not 1 <= world <= 8:
         raise ValueError("supported process count is 1..8")
     if args.command == "plan":
-        estimates = [training_estimate(model, args.batch_size, args.length, c, args.checkpoint_chunks)
-                     for c in (1, 2, 4, 8) if model.heads % c == 0]
-        kv = (2 * args.batch_size * args.length * model.dim * (2 if args.precision == "bf16" else 4)
-              if isinstance(model, StackModel) else None)
-        print(json.dumps({"model": options, "training": estimates, "inference_raw_kv_bytes": kv},
-                         indent=2))
-        return
-    if args.device == "cuda":
-        if not torch.cuda.is_available():
-            raise RuntimeError("NVIDIA CUDA is required; use --device cpu for the reference path")
-        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        device = torch.device("cuda", torch.cuda.current_device())
-        capacity = torch.cuda.mem_get_info(device)[1]
-    else:
-        device, capacity = torch.device("cpu"), 64 * GiB
+        _plan_report(args, model, options)
+        return None
+    device, capacity = _this_rank_device(args)
     if world > 1:
         init_distributed(args.device)
-        cap = torch.tensor(capacity, device=device, dtype=torch.long)
-        dist.all_reduce(cap, op=dist.ReduceOp.MIN)
-        capacity = int(cap)
+        smallest = torch.tensor(capacity, device=device, dtype=torch.long)
+        dist.all_reduce(smallest, op=dist.ReduceOp.MIN)     # plan for the smallest GPU of the job
+        capacity = int(smallest)
     cp = choose_cp(args, model, world, capacity) if args.command == "train" else 1
-    parallel = ParallelContext.initialize(cp, args.device)
+    parallel = None
     try:
+        parallel = ParallelContext.initialize(cp, args.device)
         estimate = training_estimate(model, args.batch_size, args.length, cp, args.checkpoint_chunks)
         estimate.pop("note")
-        hint = None
+        record = {"event": "configuration", "model": options, "world": world, "cp": cp, "dp": parallel.dp_size,
+                  "effective_batch": args.batch_size * parallel.dp_size * args.grad_accum, **estimate}
         if world == 1 and args.device == "cuda" and torch.cuda.device_count() > 1:
-            hint = (f"{torch.cuda.device_count()} GPUs are visible; launch with torchrun "
-                    "--nproc_per_node=N to use them")
-        emit({"event": "configuration", "model": options, "world": world, "cp": cp,
-              "dp": parallel.dp_size, "effective_batch": args.batch_size * parallel.dp_size * args.grad_accum,
-              **estimate, **({"hint": hint} if hint else {})}, args, parallel.rank)
-        if args.command == "train" and device.type == "cuda" and not args.allow_over_budget \
-                and estimate["estimated_total_bytes"] > capacity * args.memory_fraction:
+            record["hint"] = (f"{torch.cuda.device_count()} GPUs are visible; launch with torchrun "
+                              "--nproc_per_node=N to use them")
+        emit(record, args, parallel.rank)
+        over = estimate["estimated_total_bytes"] > capacity * args.memory_fraction
+        if args.command == "train" and device.type == "cuda" and over and not args.allow_over_budget:
             raise MemoryError("training estimate exceeds the memory budget; reduce the micro-batch, "
                               "use CP/recompute, or pass --allow-over-budget")
         if args.task in ("passkey", "copying", "mqar") and args.vocab_size < data.VOCAB:
             raise ValueError("synthetic tasks require vocab_size >= 128")
-        validation = None
-        if args.task == "tokens":
-            dataset = TokenDataset(args.tokens, args.token_dtype)
-            if args.validation_tokens:
-                validation = TokenDataset(args.validation_tokens, args.token_dtype)
-        elif args.task == "enwik8":
-            dataset = enwik8_dataset(args.tokens or "data/enwik8",
-                                     "train" if args.command == "train" else args.split)
-            if args.command == "train" and args.eval_every:
-                validation = enwik8_dataset(args.tokens or "data/enwik8", args.split)
-        else:
-            dataset = None
+        dataset, validation = _datasets(args)
         model.to(device)
         if device.type == "cuda" and isinstance(model, StackModel) and args.backend != "torch":
+            # NVLink exchange: symmetric heap sized for the longest sequence this run sees.
             length = max(args.length, getattr(args, "eval_length", 0) or 0)
-            parallel.attach_fused(device, max(512 << 20, parallel.fused_heap_bytes(
-                model, args.batch_size, length)))
+            parallel.attach_fused(device, max(512 << 20, parallel.fused_heap_bytes(model, args.batch_size, length)))
         if args.command == "train":
             return train(args, model, parallel, ck, dataset, validation)
         return evaluate(args, model, parallel, dataset)
     finally:
-        parallel_ctx = locals().get("parallel")
-        if parallel_ctx is not None:
-            parallel_ctx.close()
+        if parallel is not None:
+            parallel.close()
         if dist.is_initialized():
             dist.destroy_process_group()

@@ -1,10 +1,28 @@
-"""Capacity planning for training and paged inference.
+"""Memory planning for training and paged inference on a B200 node.
 
-Estimates are conservative and only used to choose a configuration or to
-refuse an obviously over-budget run; they are not throughput promises
-(reference: st/runtime/memory.py:43-112). Budgets assume a B200: 180 GB of
-HBM3e per GPU, so the GPU tier of the KV cache is the default for far longer
-contexts than on smaller parts.
+Training: :func:`training_estimate` adds up what one rank of this framework
+holds for a step, item by item, from the buffers it actually allocates:
+
+* the flat parameter state of the graph step (fp32 master weights, the fp32
+  gradient in the symmetric heap, the bf16 GEMM shadow, and AdamW's two fp32
+  moments, which ZeRO-1 divides over the data-parallel ranks);
+* the activations kept for backward per token and per layer on the native
+  path (bf16 GEMM inputs, the fp32 residual stream, the kept GELU derivative,
+  the gated-attention row statistics), or only the layer inputs when blocks
+  are recomputed;
+* the Ulysses exchange buffers of the NVLink path when CP > 1;
+* a fixed allowance for kernel workspaces, NCCL and allocator slack.
+
+It is an estimate for choosing CP and refusing runs that cannot fit, not a
+measurement (the reference's planner is st/runtime/memory.py:43-112; this one
+is derived from this framework's own buffers).
+
+Inference: :func:`plan_inference` places the raw K/V of the read rounds for
+this rank's shard in the fastest tier that holds it: device HBM (180 GB per
+B200), pinned host memory (page-locked memory is taken from a smaller share of
+the node's free RAM, divided among the node's ranks), or preallocated files.
+Every transient buffer of the streaming loops (prefill chunk, transfer page,
+score tile, head slice) is bounded by one workspace size.
 """
 from __future__ import annotations
 
@@ -17,8 +35,14 @@ import torch
 GiB = 1 << 30
 MiB = 1 << 20
 
+B200_HBM_BYTES = 183_359 * MiB          # what nvidia-smi reports for one B200
+RUNTIME_ALLOWANCE = 2 * GiB             # kernel workspaces, NCCL buffers, allocator slack
+PINNED_SHARE = 0.7                      # page-locked fraction of a rank's share of free host RAM
+CACHE_TIERS = ("auto", "cuda", "cpu", "disk")
+
 
 def available_host_memory() -> int | None:
+    """Free host RAM in bytes (``MemAvailable``), or ``None`` when it cannot be read."""
     try:
         with open("/proc/meminfo") as handle:
             for line in handle:
@@ -28,95 +52,162 @@ def available_host_memory() -> int | None:
         pass
     try:
         import psutil
-        return psutil.virtual_memory().available
     except ImportError:
         return None
+    return psutil.virtual_memory().available
 
+
+def ranks_on_this_node() -> int:
+    return max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+
+
+# ---------------------------------------------------------------------------
+# training
+# ---------------------------------------------------------------------------
+
+def _layer_counts(model):
+    if hasattr(model, "local"):
+        return len(model.local), len(model.reads)
+    return len(model.blocks), 0
+
+
+def _ffn_hidden(model) -> int:
+    layers = model.local if hasattr(model, "local") else model.blocks
+    for layer in layers:
+        return layer.ffn[0].out_features
+    return 4 * model.dim
+
+
+def activation_bytes_per_token(model, recompute: bool) -> int:
+    """Bytes kept for backward per local token, summed over all layers."""
+    d = model.dim
+    hidden = _ffn_hidden(model)
+    local_layers, read_rounds = _layer_counts(model)
+    if recompute:
+        # Only each layer's fp32 input survives; one layer is rebuilt at a time.
+        live = 2 * d + 6 * d + 2 * d + 4 * d + 4 * hidden
+        return 4 * d * (local_layers + read_rounds) + live
+    # LayerNorm outputs (bf16), QKV or q (bf16), attention output (bf16), fp32
+    # residual after attention, FFN input (bf16), GELU output and derivative
+    # (bf16, hidden wide), fp32 residual after the FFN.
+    block = 2 * d + 6 * d + 2 * d + 4 * d + 2 * d + 4 * hidden + 4 * d
+    read = block - 4 * d + 4 * d + 8 * model.heads      # q instead of QKV, fp32 row statistics per head
+    raw_kv = 4 * d if read_rounds else 0                # bf16 K and V shared by every read round
+    return local_layers * block + read_rounds * read + raw_kv
+
+
+def training_estimate(model, batch, length, cp_size=1, checkpoint_chunks=True, dp_size=1) -> dict:
+    """One rank's training footprint in bytes (see the module docstring for the items)."""
+    params = sum(p.numel() for p in model.parameters())
+    local = -(-length // (cp_size * model.block_size)) * model.block_size
+    flat_state = params * (4 + 4 + 2) + params * 8 // max(1, dp_size)
+    tokens = batch * local
+    activations = tokens * activation_bytes_per_token(model, checkpoint_chunks)
+    activations += tokens * 4 * model.lm_head.out_features                # fp32 logits of the loss slices
+    exchange = 0
+    if cp_size > 1:
+        # Head-layout q/k/v (and their gradients) over the whole sequence for
+        # this rank's heads, plus the landed sequence-layout copies.
+        exchange = tokens * model.dim * 2 * 3 * 2 + tokens * model.dim * 2 * 2
+    total = flat_state + activations + exchange + RUNTIME_ALLOWANCE
+    return {"parameters": params, "parameter_optimizer_bytes": flat_state,
+            "estimated_activation_bytes": activations, "exchange_bytes": exchange,
+            "estimated_total_bytes": total, "local_tokens": local, "context_parallel": cp_size,
+            "device_capacity_bytes": B200_HBM_BYTES,
+            "note": "Capacity estimate from this framework's buffers; measure peak memory on the target GPU."}
+
+
+# ---------------------------------------------------------------------------
+# paged inference
+# ---------------------------------------------------------------------------
 
 @dataclass
 class InferencePlan:
-    cache: str
-    cache_bytes: int
-    gpu_budget_bytes: int
-    page_tokens: int
-    encoder_chunk: int
-    query_chunk: int
-    score_tokens: int
-    head_chunk: int
+    cache: str                         # tier of the K/V: cuda, cpu (pinned) or disk
+    cache_bytes: int                   # K/V bytes of this rank's shard
+    gpu_budget_bytes: int              # device bytes the K/V may take
+    page_tokens: int                   # tokens per host/disk -> device transfer page
+    encoder_chunk: int                 # prefill tokens per encoder pass
+    query_chunk: int                   # queries per read pass
+    score_tokens: int                  # keys per block-score tile
+    head_chunk: int                    # queries per LM-head slice
     host_available_bytes: int | None
 
     def to_dict(self) -> dict:
         return asdict(self)
 
 
-def _local_processes() -> int:
-    return max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+def _device_budget(param, memory_fraction) -> int:
+    if not param.is_cuda:
+        return 0
+    free, capacity = torch.cuda.mem_get_info(param.device)
+    # ``free`` is measured with the weights resident; the runtime allowance
+    # stays free for the kernels' own buffers.
+    return max(0, min(int(capacity * memory_fraction), free - RUNTIME_ALLOWANCE))
 
 
-def plan_inference(model, batch, local_length, *, cache="auto", memory_fraction=0.8,
-                   page_tokens=65536, encoder_chunk=4096, query_chunk=16, workspace_mb=256,
-                   cache_dir=None) -> InferencePlan:
-    """Pick the KV tier (cuda -> cpu -> disk) and every streaming chunk size."""
-    if not 0 < memory_fraction < 1 or min(batch, local_length, page_tokens, encoder_chunk,
-                                          query_chunk, workspace_mb) < 1:
+def _choose_tier(cache, need, device_budget, pinned_budget, cache_dir, on_cuda) -> str:
+    if cache != "auto":
+        return cache
+    if on_cuda and need < device_budget:
+        return "cuda"
+    if pinned_budget is None:
+        # Free RAM unknown: a small cache still goes to host memory.
+        if need <= 2 * GiB:
+            return "cpu"
+    elif need < pinned_budget:
+        return "cpu"
+    if cache_dir:
+        return "disk"
+    raise MemoryError(f"the K/V shard needs {need / GiB:.2f} GiB per rank; pass --cache-dir for disk "
+                      "paging or run on more inference ranks")
+
+
+def _fit(limit_bytes, bytes_per_item, cap, multiple=1) -> int:
+    """Largest multiple of ``multiple`` (at least one) not above ``cap`` whose items fit in ``limit_bytes``."""
+    count = min(cap, limit_bytes // max(1, bytes_per_item))
+    return max(multiple, count // multiple * multiple)
+
+
+def plan_inference(model, batch, local_length, *, cache="auto", memory_fraction=0.8, page_tokens=65536,
+                   encoder_chunk=4096, query_chunk=16, workspace_mb=256, cache_dir=None) -> InferencePlan:
+    """Tier of the K/V cache and the chunk sizes of prefill and the read passes."""
+    if not 0 < memory_fraction < 1:
         raise ValueError("positive sizes and 0 < memory_fraction < 1 required")
-    if cache not in ("auto", "cuda", "cpu", "disk"):
+    if min(batch, local_length, page_tokens, encoder_chunk, query_chunk, workspace_mb) < 1:
+        raise ValueError("positive sizes and 0 < memory_fraction < 1 required")
+    if cache not in CACHE_TIERS:
         raise ValueError("cache must be auto/cuda/cpu/disk")
     param = next(model.parameters())
-    b, dim, heads = model.block_size, model.dim, model.heads
-    element = param.element_size()
-    total = 2 * batch * local_length * dim * element
-    if param.is_cuda:
-        free, capacity = torch.cuda.mem_get_info(param.device)
-        # Free memory is measured after the weights; keep slack for kernel
-        # workspaces, NCCL buffers and allocator fragmentation.
-        budget = max(0, min(int(capacity * memory_fraction), free - 2 * GiB))
-    else:
-        budget = 0
+    elem = param.element_size()
+    block, dim = model.block_size, model.dim
+    kv_bytes = 2 * batch * local_length * dim * elem
     workspace = workspace_mb * MiB
+    need = kv_bytes + 4 * workspace                  # transfer pages and score tiles in flight
+    device_budget = _device_budget(param, memory_fraction)
     host = available_host_memory()
-    host_budget = None if host is None else host / _local_processes()
-    need = total + 4 * workspace
-    if cache == "auto":
-        if param.is_cuda and need < budget:
-            cache = "cuda"
-        elif host_budget is not None and need < host_budget * 0.7:
-            cache = "cpu"
-        elif host_budget is None and need <= 2 * GiB:
-            cache = "cpu"
-        elif cache_dir:
-            cache = "disk"
-        else:
-            raise MemoryError(f"KV needs {total / GiB:.2f} GiB per rank; pass --cache-dir for disk "
-                              "paging or use more inference ranks")
-    if cache == "cuda" and (not param.is_cuda or need >= budget):
-        raise MemoryError(f"GPU KV needs {total / GiB:.2f} GiB plus workspace; use --cache auto/cpu/disk")
-    if cache == "cpu" and host_budget is not None and need > host_budget * 0.7:
-        raise MemoryError(f"CPU KV needs {total / GiB:.2f} GiB; available RAM {host / GiB:.2f} GiB")
-    if cache == "disk":
+    pinned_budget = None if host is None else int(host / ranks_on_this_node() * PINNED_SHARE)
+    tier = _choose_tier(cache, need, device_budget, pinned_budget, cache_dir, param.is_cuda)
+    if tier == "cuda" and (not param.is_cuda or need >= device_budget):
+        raise MemoryError(f"GPU K/V needs {kv_bytes / GiB:.2f} GiB plus workspace; use --cache auto/cpu/disk")
+    if tier == "cpu" and pinned_budget is not None and need > pinned_budget:
+        raise MemoryError(f"pinned K/V needs {kv_bytes / GiB:.2f} GiB; free host RAM is "
+                          f"{(host or 0) / GiB:.2f} GiB; use --cache disk")
+    if tier == "disk":
         if not cache_dir:
             raise ValueError("disk cache needs --cache-dir on a filesystem with room for the shard")
         os.makedirs(cache_dir, exist_ok=True)
-        if (total + GiB) * _local_processes() > shutil.disk_usage(cache_dir).free:
-            raise MemoryError("insufficient free disk space for the local KV shard")
-    page = max(b, min(page_tokens, workspace // max(2 * batch * dim * element, 1)) // b * b)
-    enc = max(b, min(encoder_chunk, workspace // max(24 * batch * dim * element, 1)) // b * b)
-    qc = max(1, min(query_chunk, workspace // max(batch * heads * model.topk * b * 4, 1)))
-    score = max(b, min(page, workspace // max(4 * batch * heads * qc * 4, 1)) // b * b)
-    head_chunk = max(1, min(qc, workspace // max(batch * model.lm_head.out_features * 4, 1)))
-    return InferencePlan(cache, total, budget, page, enc, qc, score, head_chunk, host)
-
-
-def training_estimate(model, batch, length, cp_size=1, checkpoint_chunks=True) -> dict:
-    """Parameter/optimizer bytes (16 B/param) plus an activation factor per layer."""
-    params = sum(p.numel() for p in model.parameters())
-    local = -(-length // (cp_size * model.block_size)) * model.block_size
-    layers = len(model.local) if hasattr(model, "local") else len(model.blocks)
-    reads = len(model.reads) if hasattr(model, "reads") else layers
-    factor = (layers * 2 + reads * 8 + 12) if checkpoint_chunks else (layers * 16 + reads * 20 + 12)
-    activations = batch * local * model.dim * 4 * factor
-    return {"parameters": params, "parameter_optimizer_bytes": params * 16,
-            "estimated_activation_bytes": activations,
-            "estimated_total_bytes": params * 16 + activations + 2 * GiB,
-            "local_tokens": local, "context_parallel": cp_size,
-            "note": "Capacity estimate; measure peak memory on the target GPU."}
+        if (kv_bytes + GiB) * ranks_on_this_node() > shutil.disk_usage(cache_dir).free:
+            raise MemoryError("insufficient free disk space for the local K/V shard")
+    heads, topk = model.heads, model.topk
+    # A transfer page holds K and V of `page` tokens; two pages are in flight.
+    page = _fit(workspace // 2, 2 * batch * dim * elem, page_tokens, block)
+    # A prefill chunk keeps about 24 activations of width `dim` per token alive.
+    enc = _fit(workspace, 24 * batch * dim * elem, encoder_chunk, block)
+    # A query gathers `topk` selected blocks of `block` keys per head (fp32 scores).
+    queries = _fit(workspace, 4 * batch * heads * topk * block, query_chunk)
+    # A score tile is fp32 logits of every query of the chunk against `score` keys.
+    score = min(page, _fit(workspace // 4, 4 * batch * heads * queries, page, block))
+    vocab = model.lm_head.out_features
+    head = _fit(workspace, 4 * batch * vocab, queries)
+    return InferencePlan(tier, kv_bytes, device_budget, page, enc, queries, score, head, host)

@@ -1,120 +1,126 @@
-"""Streaming evaluation metrics.
+"""Evaluation metrics accumulated on the device while logits stream by.
 
-Long-context evaluation produces logits one query chunk at a time and must
-never concatenate them. ``MetricAccumulator`` folds each chunk into running
-sums: cross-entropy, argmax hits, per-row error counts and optional
-absolute-position buckets (reference: st/runtime/metrics.py:47-117).
+Long-context evaluation yields logits one query chunk at a time. Each chunk is
+folded into a small table of float64 sums that stays on the device where the
+logits live: one row per absolute-position bucket (plus a row for the whole
+evaluation) with columns (summed cross-entropy, token count, argmax hits), and
+an optional per-row error count. A chunk costs a handful of kernels and no
+host synchronisation; the table is read once, in :meth:`finalize`, which
+reports loss, bits per character, perplexity, accuracy, exact match and the
+per-bucket breakdown (the fields of st/runtime/metrics.py:47-117 in the
+reference, whose accumulator reads every chunk back to the host).
 """
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
 
 import torch
 from torch.nn import functional as F
 
-_LN2 = math.log(2.0)
+_LOSS, _COUNT, _HITS = range(3)
 
 
 def tail_mask(shape_or_targets, tail_tokens: int) -> torch.Tensor:
     """Boolean ``[B, N]`` mask that supervises only the last ``tail_tokens`` columns."""
-    has_shape = hasattr(shape_or_targets, "shape")
-    shape = tuple(shape_or_targets.shape) if has_shape else tuple(shape_or_targets)
+    is_tensor = isinstance(shape_or_targets, torch.Tensor)
+    shape = tuple(shape_or_targets.shape) if is_tensor else tuple(shape_or_targets)
     if len(shape) != 2 or tail_tokens < 1:
         raise ValueError("tail supervision needs a [batch, length] shape and tail_tokens >= 1")
-    device = shape_or_targets.device if has_shape else None
-    mask = torch.zeros(shape, dtype=torch.bool, device=device)
-    mask[:, max(0, shape[1] - int(tail_tokens)):] = True
-    return mask
+    columns = torch.arange(shape[1], device=shape_or_targets.device if is_tensor else None)
+    return (columns >= shape[1] - int(tail_tokens)).expand(shape).clone()
 
 
 def default_bucket_edges(length: int, count: int = 4) -> tuple:
+    """``count`` (about) equal position buckets over ``[0, length)``; duplicate edges collapse."""
     if length < 1 or count < 1:
         raise ValueError("length and bucket count must be positive")
-    inner = [round(length * i / count) for i in range(1, count)]
-    return tuple(int(x) for x in sorted(set([0, length, *inner])))
+    return tuple(sorted({0, length, *(round(length * i / count) for i in range(1, count))}))
 
 
 def parse_bucket_edges(spec, length: int) -> tuple:
-    """``'0,1024,4096'`` -> edges; ``None``/``''``/``'auto'`` -> four even buckets."""
+    """``'0,1024,4096'`` -> edges; ``None`` / ``''`` / ``'auto'`` -> four even buckets."""
     if spec in (None, "", "auto"):
         return default_bucket_edges(length)
-    try:
-        edges = tuple(int(tok.strip()) for tok in str(spec).split(",") if tok.strip())
-    except ValueError as exc:
-        raise ValueError("metric buckets must be comma-separated integers") from exc
-    ordered = all(a < b for a, b in zip(edges, edges[1:]))
-    if len(edges) < 2 or edges[0] != 0 or edges[-1] != length or not ordered:
+    fields = [tok.strip() for tok in str(spec).split(",") if tok.strip()]
+    if not all(tok.lstrip("-").isdigit() for tok in fields):
+        raise ValueError("metric buckets must be comma-separated integers")
+    edges = tuple(int(tok) for tok in fields)
+    if len(edges) < 2 or edges[0] != 0 or edges[-1] != length or any(b <= a for a, b in zip(edges, edges[1:])):
         raise ValueError("metric buckets must increase from 0 to the evaluated length")
     return edges
 
 
-def _summary(loss_sum: float, count: int, correct: int) -> dict:
+def _rates(loss_sum: float, count: float, hits: float) -> dict:
     loss = loss_sum / count
-    return {"loss": loss, "bpc": loss / _LN2, "ppl": math.exp(min(loss, 80.0)),
-            "accuracy": correct / count}
+    return {"loss": loss, "bpc": loss / math.log(2.0), "ppl": math.exp(min(loss, 80.0)), "accuracy": hits / count}
 
 
-@dataclass
 class MetricAccumulator:
-    bucket_edges: tuple | None = None
-    loss_sum: float = 0.0
-    count: int = 0
-    correct: int = 0
-    row_errors: torch.Tensor | None = None
-    _bucket_loss: list = field(default_factory=list)
-    _bucket_count: list = field(default_factory=list)
-    _bucket_correct: list = field(default_factory=list)
+    """Streaming token metrics with optional position buckets and per-row exact match."""
+
+    def __init__(self, bucket_edges: tuple | None = None):
+        self.bucket_edges = tuple(bucket_edges) if bucket_edges is not None else None
+        self.table = None          # float64 [1 + buckets, 3] on the logits' device
+        self.row_errors = None     # int64 [batch] when rows are tracked
+        self._inner = None
 
     def start_rows(self, batch: int, device="cpu", track_rows: bool = True):
+        """Reset; with ``track_rows`` count wrong predictions per row for exact match."""
+        self.table = None
+        self._inner = None
         self.row_errors = torch.zeros(batch, dtype=torch.long, device=device) if track_rows else None
-        if self.bucket_edges is not None:
-            slots = len(self.bucket_edges) - 1
-            self._bucket_loss = [0.0] * slots
-            self._bucket_count = [0] * slots
-            self._bucket_correct = [0] * slots
+
+    def _ensure(self, device):
+        if self.table is None or self.table.device != device:
+            slots = 1 + (len(self.bucket_edges) - 1 if self.bucket_edges is not None else 0)
+            table = torch.zeros(slots, 3, dtype=torch.float64, device=device)
+            if self.table is not None:
+                table += self.table.to(device)
+            self.table = table
+            if self.bucket_edges is not None:
+                self._inner = torch.tensor(self.bucket_edges[1:-1], device=device)
 
     def update(self, logits: torch.Tensor, targets: torch.Tensor, positions: torch.Tensor | None = None):
+        """Fold one chunk: ``logits [B, Q, V]``, ``targets [B, Q]``, absolute ``positions [B, Q]``."""
         if logits.ndim != 3 or targets.shape != logits.shape[:2]:
             raise ValueError("expected logits [batch, queries, vocab] and targets [batch, queries]")
-        token_loss = F.cross_entropy(logits.float().flatten(0, 1), targets.flatten(),
-                                     reduction="none").view_as(targets)
+        if positions is not None and self.bucket_edges is not None and positions.shape != targets.shape:
+            raise ValueError("positions must match targets for bucket metrics")
+        self._ensure(logits.device)
+        targets = targets.to(logits.device)
+        token_loss = F.cross_entropy(logits.float().flatten(0, 1), targets.flatten(), reduction="none")
         hits = logits.argmax(-1).eq(targets)
-        self.loss_sum += float(token_loss.sum())
-        self.count += targets.numel()
-        self.correct += int(hits.sum())
+        values = torch.stack((token_loss.double(), torch.ones_like(token_loss, dtype=torch.float64),
+                              hits.flatten().double()), 1)
+        self.table[0] += values.sum(0)
+        if self.bucket_edges is not None and positions is not None:
+            # right=True: bucket i covers [edge_i, edge_{i+1}).
+            slot = torch.bucketize(positions.to(logits.device).flatten().contiguous(), self._inner, right=True)
+            self.table.index_add_(0, slot + 1, values)
         if self.row_errors is not None:
             self.row_errors += (~hits).sum(1).to(self.row_errors.device)
-        if self.bucket_edges is None or positions is None:
-            return
-        if positions.shape != targets.shape:
-            raise ValueError("positions must match targets for bucket metrics")
-        inner = torch.tensor(self.bucket_edges[1:-1], device=positions.device)
-        # right=True: every bucket is [lo, hi).
-        slot = torch.bucketize(positions.contiguous(), inner, right=True)
-        for i in range(len(self._bucket_count)):
-            chosen = slot == i
-            self._bucket_loss[i] += float(token_loss[chosen].sum())
-            self._bucket_count[i] += int(chosen.sum())
-            self._bucket_correct[i] += int(hits[chosen].sum())
+
+    @property
+    def count(self) -> int:
+        return 0 if self.table is None else int(self.table[0, _COUNT])
 
     def finalize(self) -> dict:
-        if self.count < 1:
+        table = None if self.table is None else self.table.cpu().tolist()
+        if not table or table[0][_COUNT] < 1:
             raise ValueError("cannot finalize metrics over zero tokens")
-        result = _summary(self.loss_sum, self.count, self.correct)
-        result["evaluated_tokens"] = self.count
+        total = table[0]
+        result = _rates(total[_LOSS], total[_COUNT], total[_HITS])
+        result["evaluated_tokens"] = int(total[_COUNT])
         if self.row_errors is not None:
             result["exact"] = float((self.row_errors == 0).sum()) / max(1, self.row_errors.numel())
         if self.bucket_edges is not None:
             buckets = []
-            for lo, hi, loss, count, correct in zip(self.bucket_edges, self.bucket_edges[1:],
-                                                    self._bucket_loss, self._bucket_count,
-                                                    self._bucket_correct):
-                entry = {"start": lo, "end": hi, "count": count}
-                if count:
-                    entry.update(_summary(loss, count, correct))
+            for (lo, hi), row in zip(zip(self.bucket_edges, self.bucket_edges[1:]), table[1:]):
+                entry = {"start": lo, "end": hi, "count": int(row[_COUNT])}
+                if row[_COUNT]:
+                    entry.update(_rates(row[_LOSS], row[_COUNT], row[_HITS]))
                 else:
-                    entry.update({"loss": None, "bpc": None, "ppl": None, "accuracy": None})
+                    entry.update(dict.fromkeys(("loss", "bpc", "ppl", "accuracy")))
                 buckets.append(entry)
             result["buckets"] = buckets
         return result

@@ -55,7 +55,7 @@ def test_gemm_plan_splits_only_few_tile_shapes():
         pytest.skip("extension not built")
     assert ext.gemm_plain_plan(1024, 1024, 8192, 148)[1] > 1
     assert ext.gemm_plain_plan(256, 1024, 8192, 148)[1] > 1
-    assert ext.gemm_plain_plan(8192, 1024, 3072, 148) == [256, 1]
+    assert ext.gemm_plain_plan(8192, 1024, 3072, 148) == [3, 1]       # CTA-pair tiles, no split
     assert ext.gemm_plain_plan(4096, 1024, 8192, 148)[1] == 1
     bn, splits = ext.gemm_plain_plan(8192, 4096, 64, 148)
     assert splits == 1
