@@ -32,7 +32,6 @@ SOURCES = [
     "attention/gated_entry.cu",
     "attention/gated_simt.cu",
     "attention/gated_tc.cu",
-    "attention/gated_tc2.cu",
     "attention/gated_tc_bwd.cu",
     "sparse/sparse_read.cu",
     "sparse/block_scores_tc.cu",

@@ -49,10 +49,6 @@ void gated_bwd_simt_launch(const at::Tensor& grad, const at::Tensor& q, const at
                            const at::Tensor& pr, const at::Tensor& zr, const at::Tensor& lse, int64_t block,
                            at::Tensor& dq, at::Tensor& dk, at::Tensor& dv);
 bool gated_tc_supported(const at::Tensor& q, int64_t block);
-bool gated_tc2_supported(const at::Tensor& q, int64_t block);
-void gated_fwd_tc2_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& pos,
-                          int64_t block, at::Tensor& out, at::Tensor& rc, at::Tensor& pr, at::Tensor& zr,
-                          at::Tensor& lse);
 void gated_fwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& pos,
                          int64_t block, at::Tensor& out, at::Tensor& rc, at::Tensor& pr, at::Tensor& zr,
                          at::Tensor& lse);
@@ -92,13 +88,7 @@ std::vector<at::Tensor> gated_attention_fwd(const at::Tensor& q, const at::Tenso
   auto zr = at::empty_like(pr);
   auto lse = at::empty_like(pr);
   if (q.numel() == 0) return {out, rc, pr, zr, lse};
-  // One query tile per CTA by default (measured faster at the training shapes);
-  // EB200_GATED_FWD=two selects the two-tile kernel (head dim 64) for comparisons.
-  const char* choice = std::getenv("EB200_GATED_FWD");
-  const bool two = choice != nullptr && std::string(choice) == "two";
-  if (two && gated_tc2_supported(q, block))
-    gated_fwd_tc2_launch(q, k, v, pos, block, out, rc, pr, zr, lse);
-  else if (gated_tc_supported(q, block))
+  if (gated_tc_supported(q, block))
     gated_fwd_tc_launch(q, k, v, pos, block, out, rc, pr, zr, lse);
   else
     gated_fwd_simt_launch(q, k, v, pos, block, out, rc, pr, zr, lse);

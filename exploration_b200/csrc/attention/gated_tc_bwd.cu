@@ -504,15 +504,23 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
 // dK/dV kernel
 // ---------------------------------------------------------------------------
 
+// Query-side stages of the dK/dV kernel: Q, dO and the P / dA tiles written
+// for the dV / dK MMAs are double-buffered when they fit (head dim 64: 224 KB
+// of shared memory), so that the next query tile's loads and S / dP MMAs do
+// not wait for the previous tile's dV / dK MMAs.
+template <int D>
+constexpr int dkv_stages() { return D <= 64 ? 2 : 1; }
+
 template <int D>
 struct alignas(1024) DkvSmem {
+  static constexpr int kStagesQ = dkv_stages<D>();
   __nv_bfloat16 k[kT * D];
   __nv_bfloat16 v[kT * D];
-  __nv_bfloat16 q[kT * D];
-  __nv_bfloat16 g[kT * D];
-  __nv_bfloat16 pt[kT * kT];    // P as [query][key], two 64-key swizzled boxes
-  __nv_bfloat16 dat[kT * kT];   // dA, same layout
-  uint64_t kv_full, qg_full, qg_free, sdp_full, pda_full, acc_done;
+  __nv_bfloat16 q[kStagesQ][kT * D];
+  __nv_bfloat16 g[kStagesQ][kT * D];
+  __nv_bfloat16 pt[kStagesQ][kT * kT];    // P as [query][key], two 64-key swizzled boxes
+  __nv_bfloat16 dat[kStagesQ][kT * kT];   // dA, same layout
+  uint64_t kv_full, qg_full[kStagesQ], qg_free[kStagesQ], sdp_full, pda_full, acc_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -532,10 +540,13 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   const int k0 = k_tile * kT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort = &sm.abort;
+  constexpr int kQS = DkvSmem<D>::kStagesQ;
   if (threadIdx.x == 0) {
     mbar_init(&sm.kv_full, 1);
-    mbar_init(&sm.qg_full, 1);
-    mbar_init(&sm.qg_free, 1);
+    for (int s = 0; s < kQS; ++s) {
+      mbar_init(&sm.qg_full[s], 1);
+      mbar_init(&sm.qg_free[s], 1);
+    }
     mbar_init(&sm.sdp_full, 1);
     mbar_init(&sm.pda_full, 128 * SPLIT);
     mbar_init(&sm.acc_done, 1);
@@ -561,30 +572,30 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       int n = 0;
       for (int i = 0; i < p.q_tiles; ++i) {
         if (!visible(i)) continue;
-        if (n > 0 && !mbar_wait(&sm.qg_free, (n - 1) & 1, abort, p.err, kSiteKvEmpty)) break;
-        mbar_expect_tx(&sm.qg_full, 2 * kT * D * 2);
+        const int s = n % kQS, use = n / kQS;
+        if (n >= kQS && !mbar_wait(&sm.qg_free[s], (use - 1) & 1, abort, p.err, kSiteKvEmpty)) break;
+        mbar_expect_tx(&sm.qg_full[s], 2 * kT * D * 2);
         for (int h = 0; h < kHalves; ++h) {
-          tma_load_4d(sm.q + h * kBox, &tq, &sm.qg_full, h * 64, head, i * kT, batch);
-          tma_load_4d(sm.g + h * kBox, &tg, &sm.qg_full, h * 64, head, i * kT, batch);
+          tma_load_4d(sm.q[s] + h * kBox, &tq, &sm.qg_full[s], h * 64, head, i * kT, batch);
+          tma_load_4d(sm.g[s] + h * kBox, &tg, &sm.qg_full[s], h * 64, head, i * kT, batch);
         }
         ++n;
       }
-      if (*abort) {
+      if (*abort) {   // let issued copies land before the CTA exits
         mbar_wait(&sm.kv_full, 0, abort, nullptr, kSiteDrain);
-        if (n > 0) mbar_wait(&sm.qg_full, (n - 1) & 1, abort, nullptr, kSiteDrain);
+        for (int m = max(0, n - kQS); m < n; ++m)
+          mbar_wait(&sm.qg_full[m % kQS], (m / kQS) & 1, abort, nullptr, kSiteDrain);
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && count > 0) {
       const uint32_t id_s = idesc_bf16(kT, kT, false, false);
       const uint32_t id_acc = idesc_bf16(kT, D, true, true);
-      const uint32_t q_addr = smem_u32(sm.q), g_addr = smem_u32(sm.g);
       const uint32_t k_addr = smem_u32(sm.k), v_addr = smem_u32(sm.v);
-      const uint32_t pt_addr = smem_u32(sm.pt), da_addr = smem_u32(sm.dat);
-      bool ok = mbar_wait(&sm.kv_full, 0, abort, p.err, kSiteKvFull);
-      for (int n = 0; ok && n < count; ++n) {
-        if (!mbar_wait(&sm.qg_full, n & 1, abort, p.err, kSiteQFull)) break;
-        tc_fence_after();
+      // S = Q K^T and dP = dO V^T of visible query tile n (stage n % kQS).
+      auto issue_sdp = [&](int n) {
+        const int s = n % kQS;
+        const uint32_t q_addr = smem_u32(sm.q[s]), g_addr = smem_u32(sm.g[s]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk / 4) * kBox * 2 + (kk % 4) * 32;
@@ -594,8 +605,12 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
                  id_s, kk > 0);
         }
         tc_commit(&sm.sdp_full);
-        if (!mbar_wait(&sm.pda_full, n & 1, abort, p.err, kSitePFull)) break;
-        tc_fence_after();
+      };
+      // dV += P^T dO and dK += dA^T Q of tile n; then its stage is free.
+      auto issue_acc = [&](int n) {
+        const int s = n % kQS;
+        const uint32_t q_addr = smem_u32(sm.q[s]), g_addr = smem_u32(sm.g[s]);
+        const uint32_t pt_addr = smem_u32(sm.pt[s]), da_addr = smem_u32(sm.dat[s]);
 #pragma unroll
         for (int kk = 0; kk < kT / 16; ++kk) {
           // A = P^T / dA^T: M = keys (MN-major, two 64-key boxes), K = 16 queries.
@@ -607,24 +622,45 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
           mma_ss(tmem + 256 + D, a_p, b_g, id_acc, acc);   // dV += P^T dO
           mma_ss(tmem + 256, a_d, b_q, id_acc, acc);       // dK += dA^T Q
         }
-        tc_commit(&sm.qg_free);
-        tc_commit(&sm.acc_done);
+        tc_commit(&sm.qg_free[s]);
+      };
+      bool ok = mbar_wait(&sm.kv_full, 0, abort, p.err, kSiteKvFull);
+      int done = 0;   // tiles whose dV / dK MMAs are issued
+      for (int n = 0; ok && n < count; ++n) {
+        if (!mbar_wait(&sm.qg_full[n % kQS], (n / kQS) & 1, abort, p.err, kSiteQFull)) break;
+        tc_fence_after();
+        issue_sdp(n);
+        // With two stages the previous tile's dV / dK run under this tile's
+        // gradient math; with one they must finish before its stage reloads.
+        if (kQS == 2 && n > 0) issue_acc(done++);
+        if (!mbar_wait(&sm.pda_full, n & 1, abort, p.err, kSitePFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (kQS == 1) issue_acc(done++);
       }
+      if (ok && done < count) issue_acc(done++);
+      if (ok) tc_commit(&sm.acc_done);
     }
   } else if (warp >= 4) {
     const int wg = (warp - 4) >> 2;
     const int row = (threadIdx.x - 128) & (kT - 1);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(((warp - 4) & 3) * 32) << 16);
     const int c_begin = SPLIT == 2 ? wg * 64 : 0, c_end = SPLIT == 2 ? c_begin + 64 : kT;
-    uint8_t* pt = reinterpret_cast<uint8_t*>(sm.pt);
-    uint8_t* dat = reinterpret_cast<uint8_t*>(sm.dat);
     bool ok = true;
     int n = 0;
     for (int i = 0; i < p.q_tiles && ok; ++i) {
       if (!visible(i)) continue;
+      const int s = n % kQS;
+      uint8_t* pt = reinterpret_cast<uint8_t*>(sm.pt[s]);
+      uint8_t* dat = reinterpret_cast<uint8_t*>(sm.dat[s]);
       RowStats st = row_stats(p, batch, head, i * kT + row);
       finish_stats<B>(st);
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.sdp_full, n & 1, abort, p.err, kSiteSFull))) {
+      // The stage's P / dA buffers are free once the dV / dK MMAs that read
+      // them (tile n - kQS) have completed.
+      const bool stage_free = n < kQS || mbar_wait(&sm.qg_free[s], ((n / kQS) - 1) & 1, abort, p.err, kSiteKvEmpty);
+      if (!__all_sync(0xffffffffu, stage_free && mbar_wait(&sm.sdp_full, n & 1, abort, p.err, kSiteSFull))) {
         ok = false;
         break;
       }
@@ -651,7 +687,7 @@ gated_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       mbar_arrive(&sm.pda_full);
       ++n;
     }
-    if (ok && count > 0) ok = mbar_wait(&sm.acc_done, (count - 1) & 1, abort, p.err, kSiteODone);
+    if (ok && count > 0) ok = mbar_wait(&sm.acc_done, 0, abort, p.err, kSiteODone);   // committed once, after the last MMA
     const bool have = __all_sync(0xffffffffu, ok) && count > 0;
     tc_fence_after();
     // Epilogue: thread = key row of the dK/dV accumulators (warp-uniform TMEM loads).

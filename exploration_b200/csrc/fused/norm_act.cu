@@ -95,13 +95,54 @@ layer_norm_bwd_dwdb_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__
   part_b[static_cast<int64_t>(split) * cols + c] = ab;
 }
 
-__global__ void column_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                  int splits, int cols, int accumulate = 0) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
-  float acc = 0.f;
-  for (int s = 0; s < splits; ++s) acc += part[static_cast<int64_t>(s) * cols + c];
-  out[c] = accumulate ? out[c] + acc : acc;
+// out_p[c] (+)= sum over s of part_p[s][c] for one or two partial arrays
+// (p < kParts). A CTA owns 32 columns; its 8 warps each sum a contiguous
+// slice of the partial rows (a warp reads 128 contiguous bytes per row), and
+// warp 0 adds the 8 slice sums in slice order, so the result does not depend
+// on scheduling. `accumulate` adds into the outputs (parameter gradients).
+constexpr int kReduceSlices = 8;
+
+template <int kParts>
+__global__ void __launch_bounds__(32 * kReduceSlices)
+column_reduce_kernel(const float* __restrict__ part0, const float* __restrict__ part1, float* __restrict__ out0,
+                     float* __restrict__ out1, int splits, int cols, int accumulate) {
+  __shared__ float slice_sum[kParts][kReduceSlices][32];
+  const int lane = threadIdx.x & 31, slice = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int per = (splits + kReduceSlices - 1) / kReduceSlices;
+  const int s0 = slice * per, s1 = min(splits, s0 + per);
+#pragma unroll
+  for (int q = 0; q < kParts; ++q) {
+    const float* part = q == 0 ? part0 : part1;
+    float acc = 0.f;
+    if (c < cols) {
+#pragma unroll 8
+      for (int s = s0; s < s1; ++s) acc += part[static_cast<int64_t>(s) * cols + c];
+    }
+    slice_sum[q][slice][lane] = acc;
+  }
+  __syncthreads();
+  if (slice == 0 && c < cols) {
+#pragma unroll
+    for (int q = 0; q < kParts; ++q) {
+      float total = 0.f;
+#pragma unroll
+      for (int k = 0; k < kReduceSlices; ++k) total += slice_sum[q][k][lane];
+      float* out = q == 0 ? out0 : out1;
+      out[c] = accumulate ? out[c] + total : total;
+    }
+  }
+}
+
+void column_sums(const float* part, float* out, int splits, int cols, bool accumulate, cudaStream_t stream) {
+  column_reduce_kernel<1><<<cdiv(cols, 32), 32 * kReduceSlices, 0, stream>>>(part, nullptr, out, nullptr, splits,
+                                                                             cols, accumulate ? 1 : 0);
+}
+
+void column_sums2(const float* part_w, const float* part_b, float* out_w, float* out_b, int splits, int cols,
+                  bool accumulate, cudaStream_t stream) {
+  column_reduce_kernel<2><<<cdiv(cols, 32), 32 * kReduceSlices, 0, stream>>>(part_w, part_b, out_w, out_b, splits,
+                                                                             cols, accumulate ? 1 : 0);
 }
 
 // Gradient of a linear layer's fp32 output: the bf16 copy the GEMMs read and
@@ -289,22 +330,6 @@ ln_bwd_vec_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__ x, const
   }
 }
 
-// out_w[c] (+)= sum_s part_w[s][c], out_b likewise (one launch for both;
-// `accumulate` adds into the outputs, e.g. straight into parameter gradients).
-__global__ void column_sum2_kernel(const float* __restrict__ part_w, const float* __restrict__ part_b,
-                                   float* __restrict__ out_w, float* __restrict__ out_b, int splits, int cols,
-                                   int accumulate = 0) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
-  float aw = 0.f, ab = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    aw += part_w[static_cast<int64_t>(s) * cols + c];
-    ab += part_b[static_cast<int64_t>(s) * cols + c];
-  }
-  out_w[c] = accumulate ? out_w[c] + aw : aw;
-  out_b[c] = accumulate ? out_b[c] + ab : ab;
-}
-
 #define EB_DISPATCH_V(V_VALUE, NAME, ...)                                   \
   switch (V_VALUE) {                                                        \
     case 1: { constexpr int NAME = 1; __VA_ARGS__(); break; }              \
@@ -472,9 +497,8 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
         });
       });
     });
-    column_sum2_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(pw.data_ptr<float>(), pb.data_ptr<float>(),
-                                                           dw.data_ptr<float>(), db.data_ptr<float>(), ctas, cols,
-                                                           acc ? 1 : 0);
+    column_sums2(pw.data_ptr<float>(), pb.data_ptr<float>(), dw.data_ptr<float>(), db.data_ptr<float>(), ctas, cols,
+                 acc, stream);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     count_launch(2);
     return {dx, dw, db};
@@ -499,12 +523,10 @@ std::vector<at::Tensor> layer_norm_bwd(const at::Tensor& dy, const at::Tensor& x
   // General widths: fresh sums, then the optional accumulations as separate adds.
   at::Tensor dw_f = acc ? at::empty({cols}, x.options().dtype(at::kFloat)) : dw;
   at::Tensor db_f = acc ? at::empty({cols}, x.options().dtype(at::kFloat)) : db;
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_w.data_ptr<float>(), dw_f.data_ptr<float>(),
-                                                         splits, cols);
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part_b.data_ptr<float>(), db_f.data_ptr<float>(),
-                                                         splits, cols);
+  column_sums2(part_w.data_ptr<float>(), part_b.data_ptr<float>(), dw_f.data_ptr<float>(), db_f.data_ptr<float>(),
+               splits, cols, false, stream);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  count_launch(4);
+  count_launch(3);
   if (acc) {
     dw.add_(dw_f);
     db.add_(db_f);
@@ -534,8 +556,7 @@ std::vector<at::Tensor> cast_colsum(const at::Tensor& x, const c10::optional<at:
   cast_colsum_kernel<<<ctas, 256, 0, stream>>>(reinterpret_cast<const float4*>(x.data_ptr()),
                                                reinterpret_cast<uint2*>(out.data_ptr()),
                                                reinterpret_cast<float4*>(part.data_ptr()), rows, cols / 4);
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part.data_ptr<float>(), sums.data_ptr<float>(), ctas, cols,
-                                                         acc ? 1 : 0);
+  column_sums(part.data_ptr<float>(), sums.data_ptr<float>(), ctas, cols, acc, stream);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(2);
   return {out, sums};
@@ -553,8 +574,7 @@ at::Tensor column_sum(const at::Tensor& part, const c10::optional<at::Tensor>& s
                 "column_sum: sum_acc must be contiguous fp32 [cols]");
   at::Tensor sums = acc ? *sum_acc : at::empty({cols}, part.options());
   if (cols == 0) return sums;
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      part.data_ptr<float>(), sums.data_ptr<float>(), splits, cols, acc ? 1 : 0);
+  column_sums(part.data_ptr<float>(), sums.data_ptr<float>(), splits, cols, acc, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(1);
   return sums;
@@ -595,8 +615,7 @@ std::vector<at::Tensor> bias_gelu_bwd(const at::Tensor& dout, const at::Tensor& 
         bias.data_ptr<float>(), reinterpret_cast<T*>(dh.data_ptr()), part.data_ptr<float>(), rows,
         cols, cdiv(rows, splits));
   });
-  column_sum_kernel<<<cdiv(cols, 256), 256, 0, stream>>>(part.data_ptr<float>(), dbias.data_ptr<float>(),
-                                                         splits, cols);
+  column_sums(part.data_ptr<float>(), dbias.data_ptr<float>(), splits, cols, false, stream);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(2);
   return {dh, dbias};

@@ -99,9 +99,6 @@ def main(argv=None):
             print(f"{name} ok errors={ext.device_errors(torch.cuda.current_device())}", flush=True)
         return
     result = {name + "_ms": round(_time(fn, args.warmup, args.iterations), 4) for name, fn in ops.items()}
-    os.environ["EB200_GATED_FWD"] = "two"
-    result["gated_fwd_two_tile_ms"] = round(_time(gated_fwd, args.warmup, args.iterations), 4)
-    os.environ.pop("EB200_GATED_FWD")
     result["shape"] = {"length": n, "heads": H, "head_dim": D, "block": b}
     print(json.dumps(result), flush=True)
 

@@ -73,3 +73,18 @@ def test_both_arms_describe_the_workload_with_the_same_keys():
     assert set(ours) == {"model", "global_batch", "seq_len", "parallelism", "activation_recompute", "l2"}
     assert ours["parallelism"] == "cp2" and ours["model"] == "stack_100m"
     assert [bench.last_window(k) for k in (1, 10, 20, 25, 100)] == [1, 10, 10, 5, 10]
+
+
+def test_step_profile_puts_kernels_in_phases():
+    from exploration_b200.tools.step_profile import phase_of
+    assert phase_of("void eb::(anonymous namespace)::gemm_tc_kernel<256, 0, 0, 6, 0, 1>(CUtensorMap_st)") == "ulysses_scatter"
+    assert phase_of("void eb::(anonymous namespace)::gemm_tc_kernel<256, 0, 1, 4, 1, 1>(x)") == "ulysses_gather"
+    assert phase_of("void eb::(anonymous namespace)::gemm_tc_kernel<256, 1, 1, 1, 0, 2>(x)") == "gemm"
+    assert phase_of("eb::(anonymous namespace)::heap_barrier_kernel(int)") == "heap_barrier"
+    assert phase_of("eb::(anonymous namespace)::grad_reduce_kernel(x)") == "grad_reduce"
+    assert phase_of("void eb::(anonymous namespace)::gated_dkv_tc_kernel<64, 16, 2>(x)") == "gated_attention"
+    assert phase_of("ncclDevKernel_AllReduce_Sum_f32_RING_LL(x)") == "nccl"
+    assert phase_of("something_else") == "other"
+    assert phase_of("void eb::(anonymous namespace)::gemm_tc_kernel<256, false, true, 0, false, 2>(x)") == "gemm"
+    assert phase_of("void eb::(anonymous namespace)::gemm_tc_kernel<256, false, false, 6, false, 1>(x)") == "ulysses_scatter"
+    assert phase_of("void eb::(anonymous namespace)::gemm_tc_kernel<256, false, true, 4, true, 1>(x)") == "ulysses_gather"

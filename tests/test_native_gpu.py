@@ -252,20 +252,6 @@ def test_block_scores_tc_matches_reference(native, keys, b, d, queries, topk, fi
     assert bool((scores[..., 1:] <= scores[..., :-1]).all())
 
 
-@pytest.mark.parametrize("n,b", [(1000, 16), (8192, 16), (700, 64), (513, 128)])
-def test_gated_forward_two_tile_kernel_matches_single(n, b, monkeypatch):
-    """The two-query-tile forward (head dim 64) equals the one-tile kernel."""
-    q, k, v, _ = _dense_inputs(n, b, 64, torch.bfloat16, queries=n, heads=2)
-    pos = torch.arange(n, device="cuda")[None].expand(2, -1).clone()
-    pos[1, n // 3:] = pos[1, n // 3:].flip(0)          # not monotone in the second row
-    pos[1, 5] = -1
-    with torch.no_grad():
-        one = dense_attention(q, k, v, pos, b, "cuda")
-        monkeypatch.setenv("EB200_GATED_FWD", "two")
-        two = dense_attention(q, k, v, pos, b, "cuda")
-    torch.testing.assert_close(two.float(), one.float(), atol=2e-2, rtol=2e-2)
-
-
 @pytest.mark.parametrize("tier", ["cuda", "cpu"])
 def test_bf16_cast_model_inference_native(tier, tmp_path):
     """Evaluation casts the model to bf16 (norm/bias parameters included); the
