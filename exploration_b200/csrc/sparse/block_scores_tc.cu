@@ -141,15 +141,19 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     const int ew = warp - 4, grp = ew >> 2, w = ew & 3;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
     const float scale2 = a.scale * 1.4426950408889634f;
-    // Running base-2 (max, sum) of this CTA's visible block scores per query;
-    // only block-owner lanes (lane % B == 0) accumulate.
-    float zm[kHalf], zs[kHalf];
+    // Running base-2 (max, sum) of this CTA's visible block scores per query.
+    // After the reductions below, lane l of a block's lane group holds query
+    // l % 8 of each group of eight query columns (lanes l and l + 8 hold the
+    // same), so the first eight lanes of every block finish one query each.
+    constexpr int kGroups = kHalf / 8;
+    float zm[kGroups], zs[kGroups];
 #pragma unroll
-    for (int c = 0; c < kHalf; ++c) {
+    for (int c = 0; c < kGroups; ++c) {
       zm[c] = kNegInf;
       zs[c] = 0.f;
     }
-    const bool owner = (lane % B) == 0;
+    const bool finisher = (lane % B) < 8;
+    const int qsel = lane & 7;
     for (int i = 0; i < count; ++i) {
       const int buf = i & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.acc_full[buf], (i >> 1) & 1, abort, a.err, kSiteSFull))) break;
@@ -170,8 +174,6 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
       tc_wait_ld();
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[buf]);                        // the values are in registers
-      // Eight query columns at a time, each reduction step issued for all
-      // eight before the next, so the shuffle latencies overlap.
 #pragma unroll
       for (int j0 = 0; j0 < kHalf; j0 += 8) {
         float x[8], m[8], e[8];
@@ -180,6 +182,8 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
           x[j] = key < a.keys ? __uint_as_float(r[j0 + j]) * scale2 : kNegInf;
           m[j] = x[j];
         }
+        // Block maxima on every lane of the block (each step for all eight
+        // columns before the next, so the shuffle latencies overlap).
 #pragma unroll
         for (int o = 1; o < B; o <<= 1) {
 #pragma unroll
@@ -187,28 +191,39 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) e[j] = m[j] == kNegInf ? 0.f : ex2(x[j] - m[j]);
+        // Block sums: plain butterfly steps down to 8 lanes, then three
+        // transposing steps, each keeping the half of the columns picked by
+        // the lane bit (and the matching maxima, which need no exchange).
 #pragma unroll
-        for (int o = 1; o < B; o <<= 1) {
+        for (int o = B / 2; o >= 8; o >>= 1) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) e[j] += __shfl_xor_sync(0xffffffffu, e[j], o);
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int jj = j0 + j;
-          const int c = grp * kHalf + jj;
-          const int p = sm.pos[c];
-          const bool visible = full && p >= 0 && gid < p / B - 1 && c < a.queries && m[j] != kNegInf;
-          if (owner && c < a.queries && g < a.groups) {
-            const float sb2 = visible ? m[j] + lg2(e[j]) : kNegInf;
-            a.scores[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.groups + g] =
-                visible ? sb2 * 0.6931471805599453f : kNegInf;
-            if (visible) {
-              if (sb2 > zm[jj]) {
-                zs[jj] = zs[jj] * ex2(zm[jj] - sb2) + 1.f;
-                zm[jj] = sb2;
-              } else {
-                zs[jj] += ex2(sb2 - zm[jj]);
-              }
+        for (int s2 = 4; s2 >= 1; s2 >>= 1) {
+          const bool upper = (lane & s2) != 0;
+#pragma unroll
+          for (int t = 0; t < s2; ++t) {
+            const float send = upper ? e[t] : e[t + s2];
+            e[t] = (upper ? e[t + s2] : e[t]) + __shfl_xor_sync(0xffffffffu, send, s2);
+            m[t] = upper ? m[t + s2] : m[t];
+          }
+        }
+        const float sum = e[0], mq = m[0];                     // query j0 + qsel of this block
+        const int c = grp * kHalf + j0 + qsel;
+        const int p = sm.pos[c];
+        const bool visible = full && p >= 0 && gid < p / B - 1 && c < a.queries && mq != kNegInf;
+        if (finisher && c < a.queries && g < a.groups) {
+          const float sb2 = visible ? mq + lg2(sum) : kNegInf;
+          a.scores[((static_cast<int64_t>(batch) * a.queries + c) * a.heads + head) * a.groups + g] =
+              visible ? sb2 * 0.6931471805599453f : kNegInf;
+          if (visible) {
+            const int gi = j0 / 8;
+            if (sb2 > zm[gi]) {
+              zs[gi] = zs[gi] * ex2(zm[gi] - sb2) + 1.f;
+              zm[gi] = sb2;
+            } else {
+              zs[gi] += ex2(sb2 - zm[gi]);
             }
           }
         }
@@ -218,11 +233,11 @@ block_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
     // 4 warps x (32 / B) owners of this warpgroup.
     constexpr int kOwners = 32 / B;
     __shared__ float zpart[2][4 * kOwners][kHalf][2];
-    if (owner) {
+    if (finisher) {
 #pragma unroll
-      for (int j = 0; j < kHalf; ++j) {
-        zpart[grp][w * kOwners + lane / B][j][0] = zm[j];
-        zpart[grp][w * kOwners + lane / B][j][1] = zs[j];
+      for (int gi = 0; gi < kGroups; ++gi) {
+        zpart[grp][w * kOwners + lane / B][gi * 8 + qsel][0] = zm[gi];
+        zpart[grp][w * kOwners + lane / B][gi * 8 + qsel][1] = zs[gi];
       }
     }
     asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -260,16 +275,54 @@ EB_DEVICE uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+constexpr int kSelPerThread = 8;                       // segment values held in registers per thread
+constexpr int kSelWarps = kSelThreads / 32;
+
+// Exclusive prefix (and total) of one count per thread over the CTA, in
+// thread order; `scratch` holds kSelWarps + 1 ints.
+EB_DEVICE int block_exclusive_scan(int value, int* scratch, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = value;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) scratch[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kSelWarps ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kSelWarps) scratch[lane] = w;      // inclusive warp totals
+    if (lane == kSelWarps - 1) scratch[kSelWarps] = w;
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? scratch[warp - 1] : 0) + incl - value;
+  total = scratch[kSelWarps];
+  __syncthreads();
+  return before;
+}
+
 // Top-k of one segment of `len` values (row `blockIdx.y`, segment `blockIdx.x`
-// of `seg_len`): radix select of the k-th largest order key, then the winners
-// sorted by (score desc, index asc). `idx_in` (nullable) maps positions to
-// the indices used for ties and output; candidates beyond `len` are padding.
+// of `seg_len`, at most kSelThreads * kSelPerThread values): the segment is
+// read once into registers (value i of the segment is element i / kSelThreads
+// of thread i % kSelThreads), a 4-pass radix select over the order-preserving
+// integer image finds the k-th largest key (each pass: a shared histogram,
+// then one warp scans the 256 digit counts), the winners are gathered by
+// prefix counts in position order (ties at the threshold: lowest positions
+// first) and sorted by (score desc, index asc) with a bitonic network.
+// `idx_in` (nullable) maps positions to the indices used for ties and output.
 __global__ void __launch_bounds__(kSelThreads)
 topk_select_kernel(const float* __restrict__ values, const int* __restrict__ idx_in, int row_len, int seg_len, int k,
                    float* __restrict__ out_v, int* __restrict__ out_i, int64_t* __restrict__ out_ids, int64_t id_base) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel_prefix;
-  __shared__ int sel_remaining, n_gt;
+  __shared__ int sel_remaining;
+  __shared__ int scan_scratch[kSelWarps + 1];
   __shared__ float cand_v[kMaxK];
   __shared__ int cand_i[kMaxK];
   const int64_t row = blockIdx.y;
@@ -278,26 +331,52 @@ topk_select_kernel(const float* __restrict__ values, const int* __restrict__ idx
   const int len = max(0, min(seg_len, row_len - lo));
   const float* x = values + row * row_len + lo;
   const int* ix = idx_in != nullptr ? idx_in + row * row_len + lo : nullptr;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kk = min(k, len);
+  uint32_t keys[kSelPerThread];
+#pragma unroll
+  for (int j = 0; j < kSelPerThread; ++j) {
+    const int i = j * kSelThreads + tid;
+    keys[j] = i < len ? order_key(x[i]) : 0u;     // 0 sorts below every real key
+  }
   uint32_t prefix = 0, mask = 0;
   int remaining = kk;
   for (int shift = 24; shift >= 0 && kk > 0; shift -= 8) {
     for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < len; i += kSelThreads) {
-      const uint32_t key = order_key(x[i]);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+#pragma unroll
+    for (int j = 0; j < kSelPerThread; ++j) {
+      const int i = j * kSelThreads + tid;
+      if (i < len && (keys[j] & mask) == prefix) atomicAdd(&hist[(keys[j] >> shift) & 255u], 1u);
     }
     __syncthreads();
-    if (tid == 0) {
-      int acc = 0, digit = 255;
-      for (; digit > 0; --digit) {
-        if (acc + static_cast<int>(hist[digit]) >= remaining) break;
-        acc += hist[digit];
+    if (warp == 0) {
+      // Counts from the top digit down: lane l holds digits 255 - 8l .. 248 - 8l.
+      int c[8], sum = 0;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        c[t] = static_cast<int>(hist[255 - (8 * lane + t)]);
+        sum += c[t];
       }
-      sel_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
-      sel_remaining = remaining - acc;
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = incl - sum;
+      // The digit where the running count (from the top) first reaches `remaining`.
+      const bool mine = excl < remaining && incl >= remaining;
+      if (mine) {
+        int acc = excl;
+        int t = 0;
+        for (; t < 7; ++t) {
+          if (acc + c[t] >= remaining) break;
+          acc += c[t];
+        }
+        sel_prefix = prefix | (static_cast<uint32_t>(255 - (8 * lane + t)) << shift);
+        sel_remaining = remaining - acc;
+      }
     }
     __syncthreads();
     prefix = sel_prefix;
@@ -305,32 +384,29 @@ topk_select_kernel(const float* __restrict__ values, const int* __restrict__ idx
     mask |= 255u << shift;
     __syncthreads();
   }
-  if (tid == 0) n_gt = 0;
-  __syncthreads();
   const int take_eq = remaining;
   const int gt_total = kk - take_eq;
-  for (int i = tid; i < len && kk > 0; i += kSelThreads) {
-    const uint32_t key = order_key(x[i]);
-    if (key > prefix) {
-      const int slot = atomicAdd(&n_gt, 1);
-      cand_v[slot] = x[i];
-      cand_i[slot] = ix != nullptr ? ix[i] : lo + i;
+  // Gather in position order: values above the threshold, then the first
+  // `take_eq` equal to it.
+  int base_gt = 0, base_eq = 0;
+#pragma unroll
+  for (int j = 0; j < kSelPerThread; ++j) {
+    const int i = j * kSelThreads + tid;
+    const bool valid = i < len && kk > 0;
+    const bool gt = valid && keys[j] > prefix, eq = valid && keys[j] == prefix;
+    int total_gt = 0, total_eq = 0;
+    const int rank_gt = block_exclusive_scan(gt ? 1 : 0, scan_scratch, total_gt);
+    const int rank_eq = block_exclusive_scan(eq ? 1 : 0, scan_scratch, total_eq);
+    if (gt) {
+      cand_v[base_gt + rank_gt] = x[i];
+      cand_i[base_gt + rank_gt] = ix != nullptr ? ix[i] : lo + i;
     }
-  }
-  __syncthreads();
-  if (tid < 32 && kk > 0) {   // ties at the threshold: lowest positions first
-    int taken = 0;
-    for (int base = 0; base < len && taken < take_eq; base += 32) {
-      const int i = base + tid;
-      const bool eq = i < len && order_key(x[i]) == prefix;
-      const unsigned ballot = __ballot_sync(0xffffffffu, eq);
-      const int before = __popc(ballot & ((1u << tid) - 1u));
-      if (eq && taken + before < take_eq) {
-        cand_v[gt_total + taken + before] = x[i];
-        cand_i[gt_total + taken + before] = ix != nullptr ? ix[i] : lo + i;
-      }
-      taken += __popc(ballot);
+    if (eq && base_eq + rank_eq < take_eq) {
+      cand_v[gt_total + base_eq + rank_eq] = x[i];
+      cand_i[gt_total + base_eq + rank_eq] = ix != nullptr ? ix[i] : lo + i;
     }
+    base_gt += total_gt;
+    base_eq += total_eq;
   }
   __syncthreads();
   int n2 = 1;
@@ -453,27 +529,36 @@ std::vector<at::Tensor> block_scores_topk_tc(const at::Tensor& q, const at::Tens
   auto ids = at::empty({batch, queries, heads, kk}, q.options().dtype(at::kLong));
   auto zr = at::empty({batch, queries, heads}, fopt);
   const int rows = batch * queries * heads;
-  // Stage 1: top-kk of each segment of kSegLen block scores; stage 2: of the candidates.
-  constexpr int kSegLen = 4096;
-  const int segs = (groups + kSegLen - 1) / kSegLen;
-  if (segs == 1) {
-    topk_select_kernel<<<dim3(1, rows), kSelThreads, 0, stream>>>(scores.data_ptr<float>(), nullptr, groups, groups,
-                                                                   static_cast<int>(kk), top.data_ptr<float>(), nullptr,
-                                                                   ids.data_ptr<int64_t>(), first / block);
-  } else {
-    auto cand_v = at::empty({rows, segs, kk}, fopt);
-    auto cand_i = at::empty({rows, segs, kk}, q.options().dtype(at::kInt));
+  // Top-kk of every segment of kSegLen scores (a selection CTA holds at most
+  // kSelThreads * kSelPerThread values), then of the segments' winners, level
+  // by level until one segment remains.
+  constexpr int kSegLen = kSelThreads * kSelPerThread;
+  at::Tensor level_v = scores, level_i;
+  int len = groups;
+  int launches = 1;
+  while (true) {
+    const int segs = (len + kSegLen - 1) / kSegLen;
+    const int* idx = level_i.defined() ? level_i.data_ptr<int>() : nullptr;
+    if (segs == 1) {
+      topk_select_kernel<<<dim3(1, rows), kSelThreads, 0, stream>>>(level_v.data_ptr<float>(), idx, len, len,
+                                                                     static_cast<int>(kk), top.data_ptr<float>(),
+                                                                     nullptr, ids.data_ptr<int64_t>(), first / block);
+      ++launches;
+      break;
+    }
+    auto next_v = at::empty({rows, segs, kk}, fopt);
+    auto next_i = at::empty({rows, segs, kk}, q.options().dtype(at::kInt));
     topk_select_kernel<<<dim3(segs, rows), kSelThreads, 0, stream>>>(
-        scores.data_ptr<float>(), nullptr, groups, kSegLen, static_cast<int>(kk), cand_v.data_ptr<float>(),
-        cand_i.data_ptr<int>(), nullptr, 0);
-    const int cand_len = static_cast<int>(segs * kk);
-    topk_select_kernel<<<dim3(1, rows), kSelThreads, 0, stream>>>(
-        cand_v.data_ptr<float>(), cand_i.data_ptr<int>(), cand_len, cand_len, static_cast<int>(kk),
-        top.data_ptr<float>(), nullptr, ids.data_ptr<int64_t>(), first / block);
+        level_v.data_ptr<float>(), idx, len, kSegLen, static_cast<int>(kk), next_v.data_ptr<float>(),
+        next_i.data_ptr<int>(), nullptr, 0);
+    ++launches;
+    level_v = next_v;
+    level_i = next_i;
+    len = static_cast<int>(segs * kk);
   }
   zr_combine_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(zr_part.data_ptr<float>(), ctas, rows, zr.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  count_launch(segs == 1 ? 3 : 4);
+  count_launch(launches + 1);
   return {top, ids, zr};
 }
 

@@ -8,10 +8,18 @@
 // inside the tile. The top-k of the tile and log Z_R of the tile are
 // reduced from the score tile on the device.
 //
-// pop: one CTA per (batch, query, head) row; its warps split the slots (2
-// local-window blocks, then the selected blocks) and keep private
-// online-softmax states that are merged at the end (flash-decoding within a
-// CTA). Selected blocks carry the gate bias s_j - log Z_R.
+// pop (bf16, blocks of 16 or 32 keys, head dim 64 or 128): split over the
+// slots of a row (2 local-window blocks, then the selected blocks). A CTA of 8
+// warps takes 8 slots of one (batch, query, head) row, one block per warp:
+// the block's keys are dotted with the query by 32 / b lanes each (16-byte
+// loads, a shuffle adds the key's parts), the block's softmax is formed in
+// registers and its values accumulate with each lane owning dim / 32
+// columns (the warp reads each value row as one coalesced line). The CTA
+// merges its warps into one normalised partial and its log-mass; a second
+// kernel merges a row's partials by their log-masses (flash decoding). About
+// 66 slots per row give 9 CTAs per row, hundreds of CTAs for 16 queries.
+// Other shapes and fp32 use one CTA per row (its warps split the slots).
+// Selected blocks carry the gate bias s_j - log Z_R.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -167,6 +175,148 @@ sparse_pop_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __r
   if (threadIdx.x == 0) lse[row] = gl > 0.f ? gm + logf(gl) : kNegInf;
 }
 
+
+constexpr int kSplitWarps = 8;
+
+EB_DEVICE void bf16x8_to_float(const uint4 raw, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(h[i]);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
+  }
+}
+
+template <int DIM, int BLK>
+__global__ void __launch_bounds__(kSplitWarps * 32)
+sparse_pop_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                        const __nv_bfloat16* __restrict__ v, const int* __restrict__ pos,
+                        const int64_t* __restrict__ ids, const float* __restrict__ sel_scores,
+                        const float* __restrict__ log_zr, float* __restrict__ part_out,
+                        float* __restrict__ part_lse, int queries, int keys, int heads, int topk, int64_t offset,
+                        int chunks) {
+  constexpr int kLanesPerKey = 32 / BLK;        // lanes sharing one key's dot product
+  constexpr int kDotDims = DIM / kLanesPerKey;  // dims per lane in the dot product
+  constexpr int kValDims = DIM / 32;            // value columns owned by a lane
+  __shared__ float s_acc[kSplitWarps][DIM];
+  __shared__ float s_ml[kSplitWarps][2];
+  const int row = blockIdx.y;                   // (batch * queries + query) * heads + head
+  const int chunk = blockIdx.x;
+  const int head = row % heads, query = (row / heads) % queries, batch = row / (heads * queries);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = pos[static_cast<int64_t>(batch) * queries + query];
+  const int slot = chunk * kSplitWarps + warp;
+  float m = kNegInf, l = 0.f, acc[kValDims];
+#pragma unroll
+  for (int i = 0; i < kValDims; ++i) acc[i] = 0.f;
+  int64_t blk = -1;
+  float bias = 0.f;
+  if (p >= 0 && slot < 2 + topk) {
+    if (slot < 2) {
+      blk = p / BLK - 1 + slot;
+    } else {
+      blk = ids[static_cast<int64_t>(row) * topk + (slot - 2)];
+      const float sc = sel_scores[static_cast<int64_t>(row) * topk + (slot - 2)];
+      if (sc == kNegInf) blk = -1;
+      bias = sc - finite_or_zero(log_zr[row]);
+    }
+  }
+  if (blk >= 0) {
+    const int key_in_block = lane / kLanesPerKey, part = lane % kLanesPerKey;
+    const int64_t token = blk * BLK + key_in_block;
+    const bool ok = token >= 0 && token <= p && token >= offset && token < offset + keys;
+    // This lane's part of the query and of its key (16-byte loads).
+    const int64_t qrow = static_cast<int64_t>(row) * DIM + part * kDotDims;
+    const int64_t krow = ((static_cast<int64_t>(batch) * keys + (ok ? token - offset : 0)) * heads + head) * DIM +
+                         part * kDotDims;
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < kDotDims; c += 8) {
+      float qf[8], kf[8];
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(q + qrow + c), qf);
+      bf16x8_to_float(ok ? *reinterpret_cast<const uint4*>(k + krow + c) : make_uint4(0u, 0u, 0u, 0u), kf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot = fmaf(qf[i], kf[i], dot);
+    }
+#pragma unroll
+    for (int o = 1; o < kLanesPerKey; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    const float logit = ok ? dot * rsqrtf(static_cast<float>(DIM)) + bias : kNegInf;
+    m = warp_max(logit);                        // the block's maximum (every key counted kLanesPerKey times)
+    if (m != kNegInf) {
+      const float w = ok ? expf(logit - m) : 0.f;
+      l = warp_sum(part == 0 ? w : 0.f);
+#pragma unroll
+      for (int key = 0; key < BLK; ++key) {
+        const float wk = __shfl_sync(0xffffffffu, w, key * kLanesPerKey);
+        if (wk == 0.f) continue;                // uniform across the warp
+        const int64_t tok = blk * BLK + key - offset;
+        const __nv_bfloat16* vrow = v + ((static_cast<int64_t>(batch) * keys + tok) * heads + head) * DIM +
+                                    lane * kValDims;
+        if constexpr (kValDims == 2) {
+          const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vrow));
+          acc[0] = fmaf(wk, x.x, acc[0]);
+          acc[1] = fmaf(wk, x.y, acc[1]);
+        } else {
+          const uint2 raw = *reinterpret_cast<const uint2*>(vrow);
+          const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+          const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+          acc[0] = fmaf(wk, x.x, acc[0]);
+          acc[1] = fmaf(wk, x.y, acc[1]);
+          acc[2] = fmaf(wk, y.x, acc[2]);
+          acc[3] = fmaf(wk, y.y, acc[3]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kValDims; ++i) s_acc[warp][lane * kValDims + i] = acc[i];
+  if (lane == 0) {
+    s_ml[warp][0] = m;
+    s_ml[warp][1] = l;
+  }
+  __syncthreads();
+  // Merge the warps (fixed order) into this chunk's normalised partial.
+  float gm = kNegInf;
+#pragma unroll
+  for (int w = 0; w < kSplitWarps; ++w) gm = fmaxf(gm, s_ml[w][0]);
+  float gl = 0.f;
+#pragma unroll
+  for (int w = 0; w < kSplitWarps; ++w)
+    if (s_ml[w][0] != kNegInf) gl += s_ml[w][1] * expf(s_ml[w][0] - gm);
+  const int64_t out_base = (static_cast<int64_t>(row) * chunks + chunk) * DIM;
+  for (int d = threadIdx.x; d < DIM; d += blockDim.x) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSplitWarps; ++w)
+      if (s_ml[w][0] != kNegInf) a += s_acc[w][d] * expf(s_ml[w][0] - gm);
+    part_out[out_base + d] = gl > 0.f ? a / gl : 0.f;
+  }
+  if (threadIdx.x == 0) part_lse[static_cast<int64_t>(row) * chunks + chunk] = gl > 0.f ? gm + logf(gl) : kNegInf;
+}
+
+// One warp per row: out = sum_c 2^... of the chunk partials weighted by their
+// log-masses (chunk order), lse = log of the total mass.
+__global__ void __launch_bounds__(256)
+sparse_pop_combine_kernel(const float* __restrict__ part_out, const float* __restrict__ part_lse,
+                          float* __restrict__ out, float* __restrict__ lse, int rows, int chunks, int dim) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* pl = part_lse + static_cast<int64_t>(row) * chunks;
+  float gm = kNegInf;
+  for (int c = 0; c < chunks; ++c) gm = fmaxf(gm, pl[c]);
+  float total = 0.f;
+  for (int c = 0; c < chunks; ++c)
+    if (pl[c] != kNegInf) total += expf(pl[c] - gm);
+  for (int d = lane; d < dim; d += 32) {
+    float a = 0.f;
+    for (int c = 0; c < chunks; ++c)
+      if (pl[c] != kNegInf) a += part_out[(static_cast<int64_t>(row) * chunks + c) * dim + d] * expf(pl[c] - gm);
+    out[static_cast<int64_t>(row) * dim + d] = total > 0.f ? a / total : 0.f;
+  }
+  if (lane == 0) lse[row] = total > 0.f ? gm + logf(total) : kNegInf;
+}
+
 }  // namespace
 
 std::vector<at::Tensor> block_scores_topk(const at::Tensor& q, const at::Tensor& k, const at::Tensor& pos,
@@ -225,8 +375,35 @@ std::vector<at::Tensor> sparse_pop(const at::Tensor& q, const at::Tensor& k, con
   auto lse = at::empty({batch, queries, heads}, q.options().dtype(at::kFloat));
   const int rows = batch * queries * heads;
   if (rows == 0) return {out, lse};
-  const size_t smem = sizeof(float) * (dim + kPopWarps * dim + kPopWarps * 2);
   auto stream = at::cuda::getCurrentCUDAStream();
+  const bool aligned = reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0;
+  if (q.scalar_type() == at::kBFloat16 && aligned && (dim == 64 || dim == 128) && (block == 16 || block == 32)) {
+    const int chunks = cdiv(2 + topk, kSplitWarps);
+    auto part_out = at::empty({rows, chunks, dim}, q.options().dtype(at::kFloat));
+    auto part_lse = at::empty({rows, chunks}, q.options().dtype(at::kFloat));
+    const dim3 grid(chunks, rows);
+    using T = __nv_bfloat16;
+    auto args = [&](auto kernel) {
+      kernel<<<grid, kSplitWarps * 32, 0, stream>>>(
+          reinterpret_cast<const T*>(q.data_ptr()), reinterpret_cast<const T*>(k.data_ptr()),
+          reinterpret_cast<const T*>(v.data_ptr()), pos.data_ptr<int>(), ids.data_ptr<int64_t>(),
+          scores.data_ptr<float>(), log_zr.data_ptr<float>(), part_out.data_ptr<float>(),
+          part_lse.data_ptr<float>(), queries, keys, heads, topk, offset, chunks);
+    };
+    if (dim == 64 && block == 16) args(sparse_pop_split_kernel<64, 16>);
+    else if (dim == 64) args(sparse_pop_split_kernel<64, 32>);
+    else if (block == 16) args(sparse_pop_split_kernel<128, 16>);
+    else args(sparse_pop_split_kernel<128, 32>);
+    sparse_pop_combine_kernel<<<cdiv(rows, 8), 256, 0, stream>>>(part_out.data_ptr<float>(), part_lse.data_ptr<float>(),
+                                                                 out.data_ptr<float>(), lse.data_ptr<float>(), rows,
+                                                                 chunks, dim);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch(2);
+    return {out, lse};
+  }
+  const size_t smem = sizeof(float) * (dim + kPopWarps * dim + kPopWarps * 2);
   if (q.scalar_type() == at::kBFloat16) {
     using T = __nv_bfloat16;
     sparse_pop_kernel<T><<<rows, kPopWarps * 32, smem, stream>>>(

@@ -193,31 +193,40 @@ def sparse_attention(q, cache, positions, block_size, topk, backend="auto", grou
     ext = _native.native(q) if native else None
     dtype = work_dtype(q)
     shape = q.shape[:3]
-    scores = torch.full((*shape, topk), NEG_INF, dtype=dtype, device=q.device)
-    ids = torch.full(scores.shape, -1, dtype=torch.int64, device=q.device)
-    log_zr = torch.full(shape, NEG_INF, dtype=dtype, device=q.device)
     tile = max(b, score_page_tokens // b * b)
     pos32 = positions.to(torch.int32).contiguous() if native else None
     qc = q.contiguous()
+    scores = ids = log_zr = None
     for first, chunk in _score_chunks(cache, q.device, tile, native):
         if native and ext.block_scores_tc_supported(qc, chunk, b, topk):
             part_scores, part_ids, part_zr = ext.block_scores_topk_tc(
                 qc, chunk.contiguous(), pos32, b, first, topk)
             record("block_scores_topk", dtype=str(q.dtype), head_dim=q.shape[-1], block=b, path="tcgen05")
-            part_scores = part_scores.to(dtype)
         elif native:
             part_scores, part_ids, part_zr = ext.block_scores_topk(
                 qc, chunk.contiguous(), pos32, b, first, topk)
             record("block_scores_topk", dtype=str(q.dtype), head_dim=q.shape[-1], block=b)
-            part_scores = part_scores.to(dtype)
         else:
             s = block_scores_reference(q, chunk, positions, b, first)
             part_zr = s.logsumexp(-1)
             count = min(topk, s.shape[-1])
             part_scores, part_ids = s.topk(count, -1)
             part_ids = part_ids + first // b
-        log_zr = torch.logaddexp(log_zr, part_zr.to(dtype))
-        scores, ids = _topk_merge(scores, ids, part_scores, part_ids.to(torch.int64), topk)
+        part_scores, part_zr, part_ids = part_scores.to(dtype), part_zr.to(dtype), part_ids.to(torch.int64)
+        if scores is None and part_scores.shape[-1] == topk:
+            # The first piece already holds k candidates per row: no merge needed.
+            scores, ids, log_zr = part_scores, part_ids, part_zr
+            continue
+        if scores is None:
+            scores = torch.full((*shape, topk), NEG_INF, dtype=dtype, device=q.device)
+            ids = torch.full(scores.shape, -1, dtype=torch.int64, device=q.device)
+            log_zr = torch.full(shape, NEG_INF, dtype=dtype, device=q.device)
+        log_zr = torch.logaddexp(log_zr, part_zr)
+        scores, ids = _topk_merge(scores, ids, part_scores, part_ids, topk)
+    if scores is None:                                   # an empty cache
+        scores = torch.full((*shape, topk), NEG_INF, dtype=dtype, device=q.device)
+        ids = torch.full(scores.shape, -1, dtype=torch.int64, device=q.device)
+        log_zr = torch.full(shape, NEG_INF, dtype=dtype, device=q.device)
     distributed = group is not None and dist.is_initialized() and dist.get_world_size(group) > 1
     if distributed:
         world = dist.get_world_size(group)
@@ -228,9 +237,9 @@ def sparse_attention(q, cache, positions, block_size, topk, backend="auto", grou
         scores, take = torch.cat(gathered_s, -1).topk(topk, -1)
         ids = torch.cat(gathered_i, -1).gather(-1, take)
         log_zr = _global_logsumexp(log_zr, group)
-    ids = ids.masked_fill(~torch.isfinite(scores), -1)
-    out = torch.zeros(q.shape, dtype=dtype, device=q.device)
-    lse = torch.full(shape, NEG_INF, dtype=dtype, device=q.device)
+    if distributed or return_selection or not native:
+        ids = ids.masked_fill(~torch.isfinite(scores), -1)   # the native pop skips -inf scores itself
+    out = lse = None
     resident = native and isinstance(cache, TensorPages) and cache.k.device == q.device
     pieces = [(cache.offset, cache.k, cache.v)] if resident else \
         cache.pages(q.device, cache.touched_pages(ids, positions, b))
@@ -243,7 +252,13 @@ def sparse_attention(q, cache, positions, block_size, topk, backend="auto", grou
             part, part_lse = part.to(dtype), part_lse.to(dtype)
         else:
             part, part_lse = pop_reference(q, keys, values, positions, ids, scores, log_zr, b, start)
-        out, lse = lse_merge(out, lse, part, part_lse)
+        if out is None:
+            out, lse = part, part_lse
+        else:
+            out, lse = lse_merge(out, lse, part, part_lse)
+    if out is None:
+        out = torch.zeros(q.shape, dtype=dtype, device=q.device)
+        lse = torch.full(shape, NEG_INF, dtype=dtype, device=q.device)
     if distributed:
         weight = torch.exp(lse - _finite_or_zero(_global_peak(lse, group)))
         out = out * weight[..., None]

@@ -80,6 +80,30 @@ def test_gated_tc_many_query_tiles(b, d):
         torch.testing.assert_close(a.float(), e, atol=3e-2 * max(1.0, scale), rtol=5e-2, msg=name)
 
 
+@pytest.mark.parametrize("b", [16, 32])
+def test_gated_tc_at_the_training_length(b):
+    """8,192 keys at head dim 64 (the stack_100m read): long key loops, the stale-max rescale,
+    sorted positions with padding rows; forward and all three gradients against the fp32 reference."""
+    torch.manual_seed(8)
+    n, heads, d = 8192, 2, 64
+    q = (torch.randn(1, n, heads, d, device="cuda") * 2).to(torch.bfloat16)
+    k = (torch.randn(1, n, heads, d, device="cuda") * 2).to(torch.bfloat16)
+    v = torch.randn(1, n, heads, d, device="cuda").to(torch.bfloat16)
+    pos = torch.arange(n, device="cuda")[None].clone()
+    pos[0, 4000:4100] = -1                                  # padding rows inside the sequence
+    q, k, v = (t.requires_grad_() for t in (q, k, v))
+    out = dense_attention(q, k, v, pos, b, "cuda")
+    rq, rk, rv = (t.detach().float().requires_grad_() for t in (q, k, v))
+    ref = dense_attention(rq, rk, rv, pos, b, "torch")
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=5e-2)
+    probe = torch.randn_like(ref)
+    got = torch.autograd.grad((out.float() * probe).sum(), (q, k, v))
+    want = torch.autograd.grad((ref * probe).sum(), (rq, rk, rv))
+    for name, a, e in zip("qkv", got, want):
+        scale = e.abs().max().item()
+        torch.testing.assert_close(a.float(), e, atol=3e-2 * max(1.0, scale), rtol=5e-2, msg=name)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("n,b,d,prev", [(37, 16, 64, False), (64, 16, 64, True), (100, 32, 32, True),
                                         (5, 8, 16, False), (130, 16, 128, True), (300, 16, 64, True),
