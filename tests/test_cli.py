@@ -1,4 +1,12 @@
-"""CLI and public API contract, including the reference's package name ``st``."""
+"""Command-line and public-API contract of this framework.
+
+The option table in ``exploration_b200.cli`` is the single definition of
+every flag, its group and the subcommands that hide it; these tests derive
+their expectations from that table instead of listing flags by hand. Runs
+go through ``main`` (the console entry point's body) on tiny CPU models.
+The contract itself is the reference's (st/cli.py:16-209, tests/test_cli.py):
+the same commands, precedence, legacy rejections and checkpoint migration.
+"""
 import contextlib
 import io
 import json
@@ -9,149 +17,177 @@ import pytest
 import torch
 
 from exploration_b200 import ExecutionConfig, ModelConfig, StackModel, build_model, load_model
-from exploration_b200.cli import entrypoint, main, parse_args
+from exploration_b200 import cli
 from exploration_b200.runtime import checkpoint
 
-CPU = ["--device", "cpu", "--backend", "torch", "--precision", "fp32"]
+CPU = ("--device", "cpu", "--backend", "torch", "--precision", "fp32")
+TINY = ("--task", "random", "--vocab-size", "31", "--dim", "16", "--heads", "2", "--block-size", "4",
+        "--arch", "L,G")
+CONFIGS = Path(__file__).resolve().parents[1] / "configs"
 
 
-def test_reference_module_aliases():
+def run(*argv):
+    """``main(argv)`` with its JSON event lines captured: (return value, events)."""
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        result = cli.main(list(argv))
+    return result, [json.loads(line) for line in out.getvalue().splitlines() if line.startswith("{")]
+
+
+def help_text(command):
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out), pytest.raises(SystemExit) as stop:
+        cli.main([command, "--help"])
+    assert stop.value.code == 0
+    return out.getvalue()
+
+
+# -- command surface --------------------------------------------------------
+
+@pytest.mark.parametrize("command", ["plan", "train", "eval"])
+def test_help_shows_exactly_the_options_the_table_makes_visible(command):
+    text = help_text(command)
+    for flag, group, kwargs in cli.OPTIONS:
+        shown = cli._visible(command, group, cli._dest(flag, kwargs))
+        # "--flag " or "--flag\n": avoid prefix matches such as --cache / --cache-dir.
+        present = any(f"{flag}{end}" in text for end in (" ", "\n", ","))
+        assert present == shown, (command, flag)
+
+
+def test_bare_invocation_lists_every_command():
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        cli.main([])
+    for command in cli.COMMANDS:
+        assert command in out.getvalue()
+
+
+def test_benchmark_and_validate_have_their_own_parsers():
+    bench, valid = help_text("benchmark"), help_text("validate")
+    assert "--compare" in bench and "--resume" not in bench
+    assert "--suite" in valid and "--dim" not in valid
+    for suite in ("reference", "resources", "cuda", "distributed"):
+        assert suite in valid
+
+
+def test_console_script_returns_nothing():
+    with patch.object(cli, "main", return_value={"loss": 0.5}) as body:
+        assert cli.entrypoint() is None
+    body.assert_called_once_with()
+
+
+def test_reference_package_name_resolves_to_these_modules():
+    import st
     import st.attention
     import st.blocks
     import st.stack_model
-    from st import data
-    from st.models import blocks, stack
-    from st.ops import attention
-    assert st.blocks is blocks
-    assert st.stack_model.StackModel is stack.StackModel
-    assert st.attention.dense_attention is attention.dense_attention
-    assert data.Q == 31 and data.KEY == 5
+    from exploration_b200.data import synthetic
+    from exploration_b200.models import blocks, stack
+    from exploration_b200.ops import attention
+    assert (st.blocks, st.stack_model.StackModel, st.attention.dense_attention) == \
+        (blocks, stack.StackModel, attention.dense_attention)
+    assert st.data.Q == synthetic.Q == 31 and st.data.KEY == synthetic.KEY == 5
 
 
-def test_scoped_help_and_no_args():
-    with contextlib.redirect_stdout(io.StringIO()) as out:
-        main([])
-    assert "benchmark" in out.getvalue()
-    for command, present, absent in (("eval", "--cache", "--grad-accum"),
-                                     ("plan", "--dim", "--eval-every"),
-                                     ("benchmark", "--compare", "--resume")):
-        with contextlib.redirect_stdout(io.StringIO()) as out, pytest.raises(SystemExit) as caught:
-            main([command, "--help"])
-        assert caught.value.code == 0
-        assert present in out.getvalue() and absent not in out.getvalue()
+# -- JSON configs and precedence -------------------------------------------
+
+@pytest.mark.parametrize("name", sorted(p.stem for p in CONFIGS.glob("*.json")))
+def test_shipped_configs_parse_and_plan(name):
+    args = cli.parse_args(["plan", "--config", str(CONFIGS / f"{name}.json")])
+    assert args.dim > 0 and args.heads > 0 and args.dim % args.heads == 0
 
 
-def test_console_entrypoint_discards_result():
-    with patch("exploration_b200.cli.main", return_value={"loss": 1.0}) as driver:
-        assert entrypoint() is None
-    driver.assert_called_once_with()
+@pytest.mark.parametrize("runtime", [{"precision": "fp16"}, {"batch_size": 2.5}, {"checkpoint_chunks": "no"},
+                                     {"command": "train"}, {"not_a_flag": 1}])
+def test_json_values_are_checked_like_flags(tmp_path, runtime):
+    path = tmp_path / "bad.json"
+    path.write_text(json.dumps({"runtime": runtime}))
+    with contextlib.redirect_stderr(io.StringIO()), pytest.raises((SystemExit, ValueError)):
+        cli.parse_args(["plan", "--config", str(path)])
 
 
-def test_json_defaults_are_validated(tmp_path):
-    path = tmp_path / "config.json"
-    for runtime in ({"precision": "fp64"}, {"batch_size": 1.5}, {"checkpoint_chunks": "false"},
-                    {"command": "eval"}):
-        path.write_text(json.dumps({"runtime": runtime}))
-        with contextlib.redirect_stderr(io.StringIO()), pytest.raises((SystemExit, ValueError)):
-            parse_args(["plan", "--config", str(path)])
+def test_flag_beats_json_beats_default(tmp_path):
+    path = tmp_path / "cfg.json"
+    path.write_text(json.dumps({"model": {"dim": 48, "heads": 6}, "runtime": {"batch_size": 3}}))
+    args = cli.parse_args(["plan", "--config", str(path), "--heads", "3"])
+    assert (args.dim, args.heads, args.batch_size, args.block_size) == (48, 3, 3, 16)
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        cli.main(["plan", "--config", str(path), "--heads", "3"])
+    planned = json.loads(out.getvalue())["model"]
+    assert (planned["heads"], planned["dim"]) == (3, 48)
 
 
-def test_public_build_load_and_legacy_checkpoint(tmp_path):
-    config = ModelConfig(vocab_size=128, dim=16, heads=2, block_size=4, arch="L,G")
-    model = build_model(config, execution=ExecutionConfig(backend="torch", encoder_chunk=8))
+@pytest.mark.parametrize("argv", [["train", "--length", str((1 << 16) + 1)], ["train", "--topk", "0"],
+                                  ["train", "--stop-exact", "0.5"], ["train", "--ema", "0.99"],
+                                  ["train", "--task", "tokens", "--eval-every", "5"]])
+def test_out_of_range_and_retired_flags_fail(argv):
+    with contextlib.redirect_stderr(io.StringIO()), pytest.raises(SystemExit):
+        cli.parse_args(argv)
+
+
+# -- public API and checkpoints ---------------------------------------------
+
+def test_build_model_then_load_a_legacy_args_checkpoint(tmp_path):
+    model = build_model(ModelConfig(vocab_size=128, dim=24, heads=3, block_size=4, arch="L,G"),
+                        execution=ExecutionConfig(backend="torch", encoder_chunk=8))
     assert isinstance(model, StackModel)
-    path = tmp_path / "legacy.pt"
-    torch.save({"model": model.state_dict(), "args": {"model": "stack", "d": 16, "heads": 2, "b": 4,
-                                                       "arch": "L,G", "task": "mqar", "read_m": 64}}, path)
-    other = load_model(path, topk=2, execution=ExecutionConfig(backend="torch", encoder_chunk=8))
-    assert other.topk == 2 and other.dim == 16 and not other.training
-    for p, q in zip(model.parameters(), other.parameters()):
-        torch.testing.assert_close(p, q, atol=0, rtol=0)
+    # Legacy files carry only the old argument names; the vocabulary follows the task (128).
+    legacy = {"model": model.state_dict(),
+              "args": {"model": "stack", "d": 24, "heads": 3, "b": 4, "arch": "L,G", "task": "passkey"}}
+    torch.save(legacy, tmp_path / "old.pt")
+    loaded = load_model(tmp_path / "old.pt", topk=3, execution=ExecutionConfig(backend="torch", encoder_chunk=8))
+    assert (loaded.topk, loaded.dim, loaded.training) == (3, 24, False)
+    for (name, a), b in zip(model.state_dict().items(), loaded.state_dict().values()):
+        assert torch.equal(a, b), name
 
+
+def test_training_loss_ignores_the_inference_topk():
+    torch.manual_seed(3)
+    execution = ExecutionConfig(backend="torch", encoder_chunk=8)
+    models = [build_model(ModelConfig(vocab_size=31, dim=16, heads=2, block_size=4, topk=k), execution=execution)
+              for k in (1, 2, 50)]
+    for other in models[1:]:
+        other.load_state_dict(models[0].state_dict())
+    ids = torch.randint(31, (2, 19))
+    targets = torch.randint(31, ids.shape)
+    losses = [m(ids, targets=targets)["loss_sum"] for m in models]
+    assert all(torch.equal(losses[0], x) for x in losses[1:])
+
+
+# -- one driver for train and eval ------------------------------------------
 
 @pytest.mark.parametrize("kind", ["stack", "baseline"])
-def test_train_eval_share_one_driver(tmp_path, kind):
-    ck = str(tmp_path / "model.pt")
-    common = ["--model", kind, "--task", "random", "--vocab-size", "31", "--dim", "16", "--heads", "2",
-              "--block-size", "4", "--arch", "L,G", "--layers", "1", "--length", "17", "--batch-size",
-              "2", "--encoder-chunk", "8", "--query-chunk", "3"]
-    with contextlib.redirect_stdout(io.StringIO()):
-        main(["train", *common, *CPU, "--steps", "2", "--grad-accum", "2", "--eval-every", "1",
-              "--save", ck])
-        result = main(["eval", "--resume", ck, "--task", "random", "--length", "23",
-                       "--eval-positions", "3", "--cache", "cpu", *CPU])
+def test_train_then_eval_a_checkpoint_of_either_model(tmp_path, kind):
+    ck = tmp_path / f"{kind}.pt"
+    _, events = run("train", "--model", kind, *TINY, "--layers", "1", "--length", "17", "--batch-size", "2",
+                    "--encoder-chunk", "8", "--query-chunk", "3", *CPU, "--steps", "2", "--grad-accum", "2",
+                    "--eval-every", "1", "--log-every", "1", "--save", str(ck))
+    assert {"train", "eval"} <= {e.get("event") for e in events}
     saved = checkpoint.load(ck)
-    assert saved["config"]["model"]["model"] == kind
-    assert saved["step"] == 1 and result["evaluated_tokens"] == 3
-    assert torch.isfinite(torch.tensor(result["loss"]))
+    assert saved["config"]["model"]["model"] == kind and saved["step"] == 1 and "ema" not in saved
+    result, _ = run("eval", "--resume", str(ck), "--task", "random", "--length", "23", "--eval-positions", "3",
+                    "--cache", "cpu", *CPU)
+    assert result["evaluated_tokens"] == 3 and torch.isfinite(torch.tensor(result["loss"]))
 
 
-def test_exact_resume_continues_the_run(tmp_path):
-    common = ["--task", "random", "--vocab-size", "31", "--dim", "16", "--heads", "2",
-              "--block-size", "4", "--arch", "L,G", "--length", "17", "--batch-size", "2",
-              "--encoder-chunk", "8", "--log-every", "1", *CPU]
-    full, part = str(tmp_path / "full.pt"), str(tmp_path / "part.pt")
-    with contextlib.redirect_stdout(io.StringIO()):
-        main(["train", *common, "--steps", "3", "--save", full])
-        main(["train", *common, "--steps", "3", "--save", part, "--save-every", "1",
-              "--stop-exact", "0", "--eval-every", "2"])
-    # The second run stopped early after step 2; resuming must land on the same weights.
-    assert checkpoint.load(part)["step"] == 1
-    with contextlib.redirect_stdout(io.StringIO()):
-        main(["train", *common, "--steps", "3", "--save", part, "--resume", part])
-    done, ref = checkpoint.load(part), checkpoint.load(full)
-    assert done["step"] == ref["step"] == 2
-    for name, value in ref["model"].items():
-        torch.testing.assert_close(done["model"][name], value, atol=0, rtol=0, msg=name)
+def test_stopped_run_resumes_onto_the_uninterrupted_weights(tmp_path):
+    common = (*TINY, "--length", "17", "--batch-size", "2", "--encoder-chunk", "8", "--log-every", "1", *CPU)
+    whole, piece = tmp_path / "whole.pt", tmp_path / "piece.pt"
+    run("train", *common, "--steps", "3", "--save", str(whole))
+    # --stop-exact 0 ends the run at its first periodic evaluation (after step 2 of 3).
+    run("train", *common, "--steps", "3", "--save", str(piece), "--save-every", "1", "--stop-exact", "0",
+        "--eval-every", "2")
+    assert checkpoint.load(piece)["step"] == 1
+    run("train", *common, "--steps", "3", "--save", str(piece), "--resume", str(piece))
+    finished, reference = checkpoint.load(piece), checkpoint.load(whole)
+    assert finished["step"] == reference["step"] == 2
+    for name, value in reference["model"].items():
+        assert torch.equal(finished["model"][name], value), name
 
 
-def test_config_round_trip_and_precedence(tmp_path):
-    path = tmp_path / "config.json"
-    path.write_text(json.dumps({"model": {"dim": 32, "heads": 4}, "runtime": {"batch_size": 2}}))
-    args = parse_args(["plan", "--config", str(path), "--dim", "16"])
-    assert args.dim == 16 and args.batch_size == 2
-    with contextlib.redirect_stdout(io.StringIO()) as output:
-        main(["plan", "--config", str(path), "--dim", "16"])
-    assert json.loads(output.getvalue())["model"]["dim"] == 16
-
-
-def test_dense_loss_does_not_depend_on_inference_topk():
-    torch.manual_seed(14)
-    execution = ExecutionConfig(backend="torch", encoder_chunk=8)
-    small = build_model(ModelConfig(vocab_size=31, dim=16, heads=2, block_size=4, topk=1),
-                        execution=execution)
-    large = build_model(ModelConfig(vocab_size=31, dim=16, heads=2, block_size=4, topk=64),
-                        execution=execution)
-    large.load_state_dict(small.state_dict())
-    ids = torch.randint(31, (1, 21))
-    targets = torch.randint(31, ids.shape)
-    torch.testing.assert_close(small(ids, targets=targets)["loss_sum"],
-                               large(ids, targets=targets)["loss_sum"], atol=0, rtol=0)
-
-
-def test_invalid_cli_and_legacy_flags_are_rejected():
-    for argv in (["train", "--length", "65537"], ["train", "--topk", "0"],
-                 ["train", "--stop-exact", ".99"], ["train", "--ema", ".9"],
-                 ["train", "--task", "tokens", "--eval-every", "1"]):
-        with contextlib.redirect_stderr(io.StringIO()), pytest.raises(SystemExit):
-            parse_args(argv)
-
-
-def test_reference_configs_parse():
-    root = Path(__file__).resolve().parents[1] / "configs"
-    for name in ("stack_2m", "stack_100m", "stack_500m", "baseline_2m"):
-        args = parse_args(["plan", "--config", str(root / f"{name}.json")])
-        assert args.dim > 0
-
-
-def test_train_profile_writes_a_trace(tmp_path):
-    out = io.StringIO()
-    common = ["--task", "random", "--vocab-size", "31", "--dim", "16", "--heads", "2", "--block-size", "4",
-              "--arch", "L,G", "--length", "17", "--batch-size", "2"]
-    with contextlib.redirect_stdout(out):
-        main(["train", *common, *CPU, "--steps", "6", "--log-every", "100", "--save", "",
-              "--profile", str(tmp_path / "prof")])
-    events = [json.loads(line) for line in out.getvalue().splitlines() if line.startswith("{")]
+def test_profile_flag_leaves_a_trace_and_a_summary(tmp_path):
+    _, events = run("train", *TINY, "--length", "17", "--batch-size", "2", *CPU, "--steps", "6",
+                    "--log-every", "100", "--save", "", "--profile", str(tmp_path / "trace"))
     profile = [e for e in events if e.get("event") == "profile"]
-    assert profile and Path(profile[0]["trace"]).exists()
-    assert profile[0]["top"]
+    assert len(profile) == 1 and Path(profile[0]["trace"]).exists() and profile[0]["top"]
