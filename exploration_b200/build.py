@@ -25,6 +25,7 @@ SOURCES = [
     "bindings.cpp",
     "fused/norm_act.cu",
     "fused/loss_optim.cu",
+    "fused/embedding.cu",
     "fused/flat_optim.cu",
     "attention/local_halo.cu",
     "attention/local_halo_b16.cu",

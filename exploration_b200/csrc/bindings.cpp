@@ -27,6 +27,7 @@ std::vector<at::Tensor> cast_colsum(const at::Tensor& x, const c10::optional<at:
 at::Tensor column_sum(const at::Tensor& part, const c10::optional<at::Tensor>& sum_acc);
 std::vector<at::Tensor> bias_gelu_bwd(const at::Tensor& dout, const at::Tensor& h, const at::Tensor& bias);
 std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets);
+at::Tensor embedding_bwd(const at::Tensor& ids, const at::Tensor& dx, int64_t vocab);
 void adamw_step(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
                 const std::vector<at::Tensor>& exp_avg, const std::vector<at::Tensor>& exp_avg_sq, double lr,
                 double beta1, double beta2, double eps, double decay, double bc1, double bc2, double grad_scale);
@@ -127,6 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("part"), py::arg("sum_acc") = py::none());
   m.def("bias_gelu_bwd", &eb::bias_gelu_bwd);
   m.def("cross_entropy_fwd", &eb::cross_entropy_fwd);
+  m.def("embedding_bwd", &eb::embedding_bwd);
   m.def("adamw_step", &eb::adamw_step);
   m.def("grad_sq_norm", &eb::grad_sq_norm);
   m.def("local_attention_supported", &eb::local_attention_supported);

@@ -59,6 +59,7 @@ using namespace sm100;
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBuckets = 256;
 constexpr int kReduceThreads = 512;
+constexpr int kLoads = 8;        // 16-byte loads in flight per thread in grad_reduce_kernel
 // Flag-slot layout (32-bit words, identical on every rank):
 //   [b * 8 + s]            rank s arrived at bucket b (epoch)
 //   [kFin + s]             rank s finished the step's reduction (epoch)
@@ -124,31 +125,48 @@ grad_reduce_kernel(PeerF32 grads, PeerFlags flags, int rank, int64_t s0, int64_t
     store_release_sys(flags.p[threadIdx.x] + bucket * 8 + rank, epoch);
   }
   if (!wait_all(flags.p[rank] + bucket * 8, W, epoch, timeout_ns, err)) return;
+  // Every thread keeps kLoads 16-byte loads in flight (U vectors from each of
+  // the W ranks) before it adds anything: a peer load takes microseconds over
+  // NVLink, and with one vector per rank 32 CTAs kept only ~256 KB in flight
+  // at W = 2 (about 110 GB/s). The ranks are still added in rank order.
+  constexpr int U = kLoads / W > 0 ? kLoads / W : 1;
   float acc = 0.f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kReduceThreads;
-  for (int64_t i = s0 / 4 + blockIdx.x * static_cast<int64_t>(kReduceThreads) + threadIdx.x; i < s1 / 4;
-       i += stride) {
-    float4 v[W];
+  const int64_t end = s1 / 4;
+  for (int64_t i0 = s0 / 4 + blockIdx.x * static_cast<int64_t>(kReduceThreads) + threadIdx.x; i0 < end;
+       i0 += stride * U) {
+    float4 v[U][W];
 #pragma unroll
-    for (int r = 0; r < W; ++r) v[r] = __ldcg(grads.p[r] + i);
-    float4 s = v[0];
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < end) {
 #pragma unroll
-    for (int r = 1; r < W; ++r) {
-      s.x += v[r].x;
-      s.y += v[r].y;
-      s.z += v[r].z;
-      s.w += v[r].w;
+        for (int r = 0; r < W; ++r) v[u][r] = __ldcg(grads.p[r] + i);
+      }
     }
-    s.x *= scale;
-    s.y *= scale;
-    s.z *= scale;
-    s.w *= scale;
-    acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
-    if (all_reduce) {
 #pragma unroll
-      for (int r = 0; r < W; ++r) grads.p[r][i] = s;
-    } else {
-      grads.p[rank][i] = s;
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= end) break;
+      float4 s = v[u][0];
+#pragma unroll
+      for (int r = 1; r < W; ++r) {
+        s.x += v[u][r].x;
+        s.y += v[u][r].y;
+        s.z += v[u][r].z;
+        s.w += v[u][r].w;
+      }
+      s.x *= scale;
+      s.y *= scale;
+      s.z *= scale;
+      s.w *= scale;
+      acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+      if (all_reduce) {
+#pragma unroll
+        for (int r = 0; r < W; ++r) grads.p[r][i] = s;
+      } else {
+        grads.p[rank][i] = s;
+      }
     }
   }
   if (all_reduce) __threadfence_system();

@@ -169,7 +169,7 @@ class StackModel(nn.Module):
 
     def encode_shard(self, input_ids, parallel, offset):
         """Embedding -> L layers (with CP halos) -> raw K/V in head layout."""
-        x = self.embedding(input_ids)
+        x = fused.embedding(input_ids, self.embedding, self.backend)
         for layer in self.local:
             halo = parallel.halo(x, self.block_size)
             x = layer(x, previous=halo, start=offset)

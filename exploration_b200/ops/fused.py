@@ -365,6 +365,38 @@ def local_attention(qkv, qkv_prev, start, valid_start, n, block, heads, backend=
 
 
 # ----------------------------------------------------------------------------
+# token embedding
+# ----------------------------------------------------------------------------
+
+
+class _EmbeddingNative(torch.autograd.Function):
+    """Row lookup; the weight gradient comes from ``embedding_bwd`` (per-vocabulary-row
+    sums in token order: deterministic, no sort of the ids)."""
+
+    @staticmethod
+    def forward(ctx, ids, weight):
+        ctx.save_for_backward(ids)
+        ctx.vocab = weight.shape[0]
+        return F.embedding(ids, weight)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad):
+        (ids,) = ctx.saved_tensors
+        ext = _native.native(grad)
+        return None, ext.embedding_bwd(ids, grad.float(), ctx.vocab)
+
+
+def embedding(ids, table: torch.nn.Embedding, backend: str = "auto"):
+    """``table(ids)``; on the native path its weight gradient avoids PyTorch's sort-based backward."""
+    w = table.weight
+    if (ids.is_cuda and backend != "torch" and w.dtype == torch.float32 and w.requires_grad
+            and w.shape[1] % 4 == 0 and table.padding_idx is None and torch.is_grad_enabled()):
+        return _EmbeddingNative.apply(ids, w)
+    return table(ids)
+
+
+# ----------------------------------------------------------------------------
 # LM head + cross entropy
 # ----------------------------------------------------------------------------
 

@@ -179,6 +179,20 @@ def test_bias_gelu_and_cross_entropy(native):
                                torch.autograd.grad(ref * 0.5, logits)[0], atol=1e-6, rtol=1e-5)
 
 
+@pytest.mark.parametrize("tokens, vocab, dim", [(8192, 256, 1024), (8193 + 8192, 31, 64), (37, 300, 1028)])
+def test_embedding_gradient_matches_torch(tokens, vocab, dim):
+    torch.manual_seed(5)
+    table = torch.nn.Embedding(vocab, dim, device="cuda")
+    ids = torch.randint(vocab, (1, tokens), device="cuda")
+    ids[0, : tokens // 3] = 3                      # one very frequent id
+    g = torch.randn(1, tokens, dim, device="cuda")
+    fused.embedding(ids, table, "cuda").backward(g)
+    ours = table.weight.grad.clone()
+    table.weight.grad = None
+    table(ids).backward(g)
+    torch.testing.assert_close(ours, table.weight.grad, atol=1e-4, rtol=1e-5)
+
+
 def test_fused_adamw_matches_torch(native):
     from exploration_b200.runtime.optim import FusedAdamW
     torch.manual_seed(2)
