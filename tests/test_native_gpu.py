@@ -129,6 +129,30 @@ def test_local_attention_matches_reference(n, b, d, prev, dtype):
         torch.testing.assert_close(a.double(), e, atol=atol * 4, rtol=rtol)
 
 
+@pytest.mark.parametrize("prev", [False, True])
+def test_local_tc_many_units_per_cta(prev):
+    """The tensor-core local kernels are persistent: with ~1,000 units of 128 rows every
+    CTA runs several, so shared-memory stages and TMEM buffers are reused."""
+    torch.manual_seed(11)
+    b, d, heads, n, start = 16, 64, 16, 4100, 32
+    qkv = torch.randn(2, n, 3, heads, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    halo = torch.randn(2, b, 3, heads, d, device="cuda", dtype=torch.bfloat16, requires_grad=True) if prev else None
+    valid = start - b if prev else start
+    out = fused.local_attention(qkv, halo, start, valid, n, b, heads, "cuda")
+    r_qkv = qkv.detach().float().requires_grad_()
+    r_halo = halo.detach().float().requires_grad_() if prev else None
+    ref = fused.local_attention_reference(r_qkv, r_halo, start, valid, n, b, heads)
+    atol, rtol = TOL[torch.bfloat16]
+    torch.testing.assert_close(out.float(), ref, atol=atol, rtol=rtol)
+    probe = torch.randn_like(out)
+    inputs = (qkv, halo) if prev else (qkv,)
+    r_inputs = (r_qkv, r_halo) if prev else (r_qkv,)
+    got = torch.autograd.grad((out * probe).sum(), inputs)
+    want = torch.autograd.grad((ref * probe.float()).sum(), r_inputs)
+    for a, e in zip(got, want):
+        torch.testing.assert_close(a.float(), e, atol=atol * 4, rtol=rtol)
+
+
 @pytest.mark.parametrize("cols,rows", [(1000, 300), (1024, 517), (768, 64), (128, 3), (1536, 200)])
 @pytest.mark.parametrize("dtype,out", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
                                        (torch.bfloat16, torch.bfloat16)])
