@@ -52,6 +52,8 @@ constexpr int kB = 16;
 constexpr int kD = 64;
 constexpr int kM = 128;                 // query rows per CTA
 constexpr int kKeys = kM + kB;          // 144 key rows per CTA
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kOCol = 160;
 constexpr int kTable = kM + 2 * kB;     // rotation offsets 0 .. 159
 constexpr float kLog2e = 1.4426950408889634f;
@@ -365,14 +367,12 @@ local_tc_fwd_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_con
 // ---------------------------------------------------------------------------
 // backward
 //
-// dQ kernel (query owner), persistent like the forward (unit = 128 query
-//   rows of one (batch, head); shared-memory stage i % 3, TMEM buffer and
-//   compute warpgroup i % 2): S = Q K^T and dP = dO V^T (128 x 144 each,
-//   sequentially in the same TMEM columns; warp 1 issues both), P = exp(S -
-//   lse) from the forward's log-sum-exp, dS = P (dP - delta) on the 32-key
-//   window (bf16 into TMEM), dQ = dS K (A-from-TMEM, issued by warp 3), then
-//   RoPE is undone on dQ. delta = rowsum(dO o O) is formed here and stored
-//   for the key kernel.
+// dQ kernel (query owner), one CTA = 128 query rows of one (batch, head):
+//   S = Q K^T and dP = dO V^T (128 x 144 each, sequentially in the same TMEM
+//   columns), P = exp(S - lse) from the forward's log-sum-exp, dS = P (dP -
+//   delta) on the 32-key window (bf16 into TMEM), dQ = dS K (A-from-TMEM),
+//   then RoPE is undone on dQ. delta = rowsum(dO o O) is formed here and
+//   stored for the key kernel.
 // dK/dV kernel (key owner), one CTA = 128 key rows [s0, s0+128); its
 //   queries are [s0, s0+144) (the next block also sees the last key block):
 //   S^T = K Q^T and dP^T = V dO^T (128 x 144), P^T and dS^T on the window,
@@ -396,15 +396,12 @@ struct LtBwdArgs {
   ErrorSlot* err;
 };
 
-constexpr int kDqStages = 3;
-
 struct alignas(1024) LtDqSmem {
-  __nv_bfloat16 q[kDqStages][kM * kD];
-  __nv_bfloat16 g[kDqStages][kM * kD];     // dO
-  __nv_bfloat16 k[kDqStages][kKeys * kD];
-  __nv_bfloat16 v[kDqStages][kKeys * kD];
-  uint64_t q_full[kDqStages], g_full[kDqStages], k_full[kDqStages], v_full[kDqStages], stage_free[kDqStages];
-  uint64_t rot_done[2], s_full[2], s_read[2], dp_full[2], ds_full[2], dq_full[2], tmem_free[2];
+  __nv_bfloat16 q[kM * kD];
+  __nv_bfloat16 g[kM * kD];     // dO
+  __nv_bfloat16 k[kKeys * kD];
+  __nv_bfloat16 v[kKeys * kD];
+  uint64_t q_full, g_full, k_full, v_full, rot_done, s_full, s_read, dp_full, ds_full, dq_full;
   uint32_t tmem_base;
   int abort;
 };
@@ -482,37 +479,32 @@ EB_DEVICE void store_band_bf16(uint32_t addr, int w, const float (&x)[48]) {
   }
 }
 
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 local_tc_dq_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_constant__ CUtensorMap t_halo,
                    const __grid_constant__ CUtensorMap t_prev, const __grid_constant__ CUtensorMap t_dout,
-                   LtBwdArgs a, int units, int tiles) {
+                   LtBwdArgs a) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
   LtDqSmem& sm = *reinterpret_cast<LtDqSmem*>((reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int first = blockIdx.x, step = gridDim.x;
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int t0 = blockIdx.x * kM;
   const int H = a.heads;
   volatile int* abort = &sm.abort;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDqStages; ++s) {
-      mbar_init(&sm.q_full[s], 1);
-      mbar_init(&sm.g_full[s], 1);
-      mbar_init(&sm.k_full[s], 1);
-      mbar_init(&sm.v_full[s], 1);
-      mbar_init(&sm.stage_free[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.rot_done[b], 128);
-      mbar_init(&sm.s_full[b], 1);
-      mbar_init(&sm.s_read[b], 128);
-      mbar_init(&sm.dp_full[b], 1);
-      mbar_init(&sm.ds_full[b], 128);
-      mbar_init(&sm.dq_full[b], 1);
-      mbar_init(&sm.tmem_free[b], 128);
-    }
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.g_full, 1);
+    mbar_init(&sm.k_full, 1);
+    mbar_init(&sm.v_full, 1);
+    mbar_init(&sm.rot_done, 128);
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_read, 128);
+    mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.dq_full, 1);
     sm.abort = 0;
     fence_barrier_init();
   }
-  if (warp == 2) tmem_alloc(&sm.tmem_base, 2 * kFwdBuf);
+  if (warp == 2) tmem_alloc(&sm.tmem_base, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -523,176 +515,139 @@ local_tc_dq_kernel(const __grid_constant__ CUtensorMap t_main, const __grid_cons
       prefetch_tensormap(&t_main);
       prefetch_tensormap(&t_halo);
       prefetch_tensormap(&t_dout);
-      if (a.has_prev) prefetch_tensormap(&t_prev);
-      int issued = 0;
-      for (int i = 0, u = first; u < units; u += step, ++i) {
-        const int s = i % kDqStages;
-        if (i >= kDqStages &&
-            !mbar_wait(&sm.stage_free[s], ((i / kDqStages) - 1) & 1, abort, a.err, kSiteKvEmpty))
-          break;
-        const LtUnit x = unit_of(u, tiles, H);
-        const bool from_prev = x.t0 == 0 && a.has_prev;
-        mbar_expect_tx(&sm.q_full[s], kM * kD * 2);
-        tma_load_4d(sm.q[s], &t_main, &sm.q_full[s], 0, x.head, x.t0, x.batch);
-        mbar_expect_tx(&sm.g_full[s], kM * kD * 2);
-        tma_load_4d(sm.g[s], &t_dout, &sm.g_full[s], 0, x.head, x.t0, x.batch);
-        for (int part = 1; part <= 2; ++part) {
-          uint64_t* bar = part == 1 ? &sm.k_full[s] : &sm.v_full[s];
-          __nv_bfloat16* dst = part == 1 ? sm.k[s] : sm.v[s];
-          mbar_expect_tx(bar, kKeys * kD * 2);
-          if (from_prev) tma_load_4d(dst, &t_prev, bar, 0, part * H + x.head, 0, x.batch);
-          else tma_load_4d(dst, &t_halo, bar, 0, part * H + x.head, x.t0 - kB, x.batch);
-          tma_load_4d(dst + kB * kD, &t_main, bar, 0, part * H + x.head, x.t0, x.batch);
-        }
-        ++issued;
-      }
-      if (*abort) {   // let this CTA's copies in flight land before it exits
-        for (int i = issued > kDqStages ? issued - kDqStages : 0; i < issued; ++i) {
-          const int s = i % kDqStages;
-          const uint32_t ph = (i / kDqStages) & 1;
-          mbar_wait(&sm.q_full[s], ph, abort, nullptr, kSiteDrain);
-          mbar_wait(&sm.g_full[s], ph, abort, nullptr, kSiteDrain);
-          mbar_wait(&sm.k_full[s], ph, abort, nullptr, kSiteDrain);
-          mbar_wait(&sm.v_full[s], ph, abort, nullptr, kSiteDrain);
-        }
+      const bool from_prev = t0 == 0 && a.has_prev;
+      mbar_expect_tx(&sm.q_full, kM * kD * 2);
+      tma_load_4d(sm.q, &t_main, &sm.q_full, 0, head, t0, batch);
+      mbar_expect_tx(&sm.g_full, kM * kD * 2);
+      tma_load_4d(sm.g, &t_dout, &sm.g_full, 0, head, t0, batch);
+      for (int part = 1; part <= 2; ++part) {
+        uint64_t* bar = part == 1 ? &sm.k_full : &sm.v_full;
+        __nv_bfloat16* dst = part == 1 ? sm.k : sm.v;
+        mbar_expect_tx(bar, kKeys * kD * 2);
+        if (from_prev) tma_load_4d(dst, &t_prev, bar, 0, part * H + head, 0, batch);
+        else tma_load_4d(dst, &t_halo, bar, 0, part * H + head, t0 - kB, batch);
+        tma_load_4d(dst + kB * kD, &t_main, bar, 0, part * H + head, t0, batch);
       }
     }
   } else if (warp == 1) {
-    // S = Q K^T, then (once the warpgroup holds P) dP = dO V^T in the same columns.
     if (lane == 0) {
       const uint32_t id_s = idesc_bf16(kM, kKeys, false, false);
-      for (int i = 0, u = first; u < units; u += step, ++i) {
-        const int s = i % kDqStages, b = i & 1, j = i >> 1;
-        const uint32_t ph = (i / kDqStages) & 1;
-        const uint32_t buf = tmem + b * kFwdBuf;
-        if (!mbar_wait(&sm.rot_done[b], j & 1, abort, a.err, kSiteQFull)) break;
-        if (i >= 2 && !mbar_wait(&sm.tmem_free[b], (j - 1) & 1, abort, a.err, kSiteODone)) break;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sm.q[s]), k_addr = smem_u32(sm.k[s]);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(buf, smem_desc_sw128(q_addr + kk * 32, 16, 1024), smem_desc_sw128(k_addr + kk * 32, 16, 1024), id_s,
-                 kk > 0);
-        tc_commit(&sm.s_full[b]);
-        if (!(mbar_wait(&sm.g_full[s], ph, abort, a.err, kSiteKvFull) &&
-              mbar_wait(&sm.v_full[s], ph, abort, a.err, kSiteKvFull) &&
-              mbar_wait(&sm.s_read[b], j & 1, abort, a.err, kSitePFull)))
-          break;
-        tc_fence_after();
-        const uint32_t g_addr = smem_u32(sm.g[s]), v_addr = smem_u32(sm.v[s]);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(buf, smem_desc_sw128(g_addr + kk * 32, 16, 1024), smem_desc_sw128(v_addr + kk * 32, 16, 1024), id_s,
-                 kk > 0);
-        tc_commit(&sm.dp_full[b]);
-      }
-    }
-  } else if (warp == 3) {
-    // dQ = dS K; its completion also frees the stage (every MMA of the unit is done).
-    if (lane == 0) {
       const uint32_t id_dq = idesc_bf16(kM, kD, false, true);
-      for (int i = 0, u = first; u < units; u += step, ++i) {
-        const int s = i % kDqStages, b = i & 1, j = i >> 1;
-        if (!mbar_wait(&sm.ds_full[b], j & 1, abort, a.err, kSitePFull)) break;
+      bool ok = mbar_wait(&sm.rot_done, 0, abort, a.err, kSiteQFull);
+      if (ok) {
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[s]);
-        const uint32_t buf = tmem + b * kFwdBuf;
+        const uint32_t q_addr = smem_u32(sm.q), k_addr = smem_u32(sm.k);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem, smem_desc_sw128(q_addr + kk * 32, 16, 1024), smem_desc_sw128(k_addr + kk * 32, 16, 1024), id_s,
+                 kk > 0);
+        tc_commit(&sm.s_full);
+        ok = mbar_wait(&sm.g_full, 0, abort, a.err, kSiteKvFull) && mbar_wait(&sm.v_full, 0, abort, a.err, kSiteKvFull) &&
+             mbar_wait(&sm.s_read, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t g_addr = smem_u32(sm.g), v_addr = smem_u32(sm.v);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tmem, smem_desc_sw128(g_addr + kk * 32, 16, 1024), smem_desc_sw128(v_addr + kk * 32, 16, 1024), id_s,
+                 kk > 0);
+        tc_commit(&sm.dp_full);
+        ok = mbar_wait(&sm.ds_full, 0, abort, a.err, kSitePFull);
+      }
+      if (ok) {
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k);
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk)
-          mma_ts(buf + kOCol, buf + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kKeys * 128, 1024), id_dq, kk > 0);
-        tc_commit(&sm.dq_full[b]);
-        tc_commit(&sm.stage_free[s]);
+          mma_ts(tmem + kOCol, tmem + kk * 8, smem_desc_sw128(k_addr + kk * 2048, kKeys * 128, 1024), id_dq, kk > 0);
+        tc_commit(&sm.dq_full);
       }
     }
   } else if (warp >= 4) {
-    const int grp = (warp - 4) >> 2;            // this warpgroup takes iterations i = grp, grp + 2, ...
-    const int w = warp & 3;
-    const int tid = threadIdx.x - 128 - grp * 128;
-    const int r = tid;
-    const int off = lane >= 16 ? kB : 0;
-    for (int i = grp, u = first + grp * step; u < units; u += 2 * step, i += 2) {
-      const int s = i % kDqStages, j = i >> 1;
-      const uint32_t ph = (i / kDqStages) & 1;
-      const uint32_t lane_addr = tmem + grp * kFwdBuf + (static_cast<uint32_t>(w * 32) << 16);
-      const LtUnit x = unit_of(u, tiles, H);
-      const int t0 = x.t0, t = t0 + r;
-      const bool row_ok = t < a.n;
-      // Row statistics first (global loads in flight while the tiles land):
-      // lse (base 2) and delta = dO . O (stored for the key kernel).
-      float lse2 = 0.f, delta = 0.f;
-      if (row_ok) {
-        const int64_t sr = (static_cast<int64_t>(x.batch) * a.n + t) * H + x.head;
-        const float l = a.lse[sr];
-        lse2 = l == kNegInf ? 0.f : l * kLog2e;
-        const uint4* go = reinterpret_cast<const uint4*>(a.dout + sr * kD);
-        const uint4* oo = reinterpret_cast<const uint4*>(a.out + sr * kD);
+    const int tid = threadIdx.x - 128;
+    const int w = warp - 4;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(w * 32) << 16);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, abort, a.err, kSiteQFull));
+    if (ok) rotate_tile<kM>(sm.q, kB, a.cos, a.sin, tid);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.k_full, 0, abort, a.err, kSiteKvFull));
+    if (ok) rotate_tile<kKeys>(sm.k, 0, a.cos, a.sin, tid);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive(&sm.rot_done);
+    // Row statistics: lse (base 2) and delta = dO . O (stored for the key kernel).
+    const int r = tid, t = t0 + r;
+    const bool row_ok = t < a.n;
+    float lse2 = 0.f, delta = 0.f;
+    if (row_ok) {
+      const int64_t s = (static_cast<int64_t>(batch) * a.n + t) * H + head;
+      const float l = a.lse[s];
+      lse2 = l == kNegInf ? 0.f : l * kLog2e;
+      const uint4* go = reinterpret_cast<const uint4*>(a.dout + s * kD);
+      const uint4* oo = reinterpret_cast<const uint4*>(a.out + s * kD);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 gu = go[c], ou = oo[c];
-          const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gu);
-          const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&ou);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 gu = go[c], ou = oo[c];
+        const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gu);
+        const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&ou);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 gf = __bfloat1622float2(gp[e]), of = __bfloat1622float2(op[e]);
-            delta += gf.x * of.x + gf.y * of.y;
-          }
-        }
-        a.delta[sr] = delta;
-      }
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full[s], ph, abort, a.err, kSiteQFull));
-      if (ok) rotate_tile<kM>(sm.q[s], kB, a.cos, a.sin, tid);
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.k_full[s], ph, abort, a.err, kSiteKvFull));
-      if (ok) rotate_tile<kKeys>(sm.k[s], 0, a.cos, a.sin, tid);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&sm.rot_done[grp]);
-      float p[48];
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.s_full[grp], j & 1, abort, a.err, kSiteSFull));
-      if (ok) {
-        tc_fence_after();
-        float xs[48];
-        load_band48(lane_addr + 32 * w, xs);
-        const float scale = 0.125f * kLog2e;
-#pragma unroll
-        for (int jj = 0; jj < 48; ++jj) {
-          const int kk = 32 * w + jj;
-          const bool in = row_ok && jj >= off && jj < off + 2 * kB && kk <= r + kB && bwd_key_ok(a, t0 - kB + kk);
-          p[jj] = in ? ex2(fmaf(xs[jj], scale, -lse2)) : 0.f;
+        for (int i = 0; i < 4; ++i) {
+          const float2 gf = __bfloat1622float2(gp[i]), of = __bfloat1622float2(op[i]);
+          delta += gf.x * of.x + gf.y * of.y;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_read[grp]);
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dp_full[grp], j & 1, abort, a.err, kSiteSFull));
-      if (ok) {
-        tc_fence_after();
-        float dp[48];
-        load_band48(lane_addr + 32 * w, dp);
-#pragma unroll
-        for (int jj = 0; jj < 48; ++jj) dp[jj] = p[jj] * (dp[jj] - delta);
-        store_band_bf16(lane_addr, w, dp);
-        tc_wait_st();
-      }
-      tc_fence_before();
-      mbar_arrive(&sm.ds_full[grp]);
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dq_full[grp], j & 1, abort, a.err, kSiteODone));
-      float y[64];
-      if (ok) {
-        tc_fence_after();
-        load_tmem64(lane_addr + kOCol, y);
-      }
-      tc_fence_before();
-      mbar_arrive(&sm.tmem_free[grp]);
-      if (!ok) break;
-#pragma unroll
-      for (int e = 0; e < 64; ++e) y[e] *= 0.125f;
-      unrotate_row(y, r + kB, a.cos, a.sin);
-      if (row_ok) store_row64(a.dqkv + ((static_cast<int64_t>(x.batch) * a.n + t) * 3 * H + x.head) * kD, y);
+      a.delta[s] = delta;
     }
+    const int off = lane >= 16 ? kB : 0;
+    float p[48];
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.s_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      float x[48];
+      load_band48(lane_addr + 32 * w, x);
+      const float scale = 0.125f * kLog2e;
+#pragma unroll
+      for (int j = 0; j < 48; ++j) {
+        const int kk = 32 * w + j;
+        const bool in = row_ok && j >= off && j < off + 2 * kB && kk <= r + kB && bwd_key_ok(a, t0 - kB + kk);
+        p[j] = in ? ex2(fmaf(x[j], scale, -lse2)) : 0.f;
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.s_read);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, 0, abort, a.err, kSiteSFull));
+    if (ok) {
+      tc_fence_after();
+      float dp[48];
+      load_band48(lane_addr + 32 * w, dp);
+#pragma unroll
+      for (int j = 0; j < 48; ++j) dp[j] = p[j] * (dp[j] - delta);
+      store_band_bf16(lane_addr, w, dp);
+      tc_wait_st();
+    }
+    tc_fence_before();
+    mbar_arrive(&sm.ds_full);
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(&sm.dq_full, 0, abort, a.err, kSiteODone));
+    if (ok) {
+      tc_fence_after();
+      float y[64];
+      load_tmem64(lane_addr + kOCol, y);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) y[i] *= 0.125f;
+      unrotate_row(y, r + kB, a.cos, a.sin);
+      if (row_ok) store_row64(a.dqkv + ((static_cast<int64_t>(batch) * a.n + t) * 3 * H + head) * kD, y);
+    }
+  }
+  if (warp == 0 && lane == 0 && *abort) {
+    mbar_wait(&sm.q_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.g_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.k_full, 0, abort, nullptr, kSiteDrain);
+    mbar_wait(&sm.v_full, 0, abort, nullptr, kSiteDrain);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * kFwdBuf);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -1086,14 +1041,13 @@ std::vector<at::Tensor> local_tc_bwd(const at::Tensor& dout, const at::Tensor& q
   };
   trace("start");
   {
-    // Persistent: one CTA per SM (all 512 TMEM columns, three shared-memory stages).
-    const size_t smem = sizeof(LtDqSmem) + 1024;
+    const size_t smem = std::max<size_t>(sizeof(LtDqSmem) + 1024, 80 * 1024);
     auto kernel = local_tc_dq_kernel;
     EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    // Two CTAs per SM need the maximum shared-memory carveout.
+    EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     trace("dq attribute");
-    const int units = ctas * heads * batch;
-    const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-    kernel<<<std::min(units, sms), kFwdThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout, args, units, ctas);
+    kernel<<<dim3(ctas, heads, batch), kThreads, smem, stream>>>(t_main, t_halo, t_prev, t_dout, args);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     trace("dq kernel");
   }

@@ -131,7 +131,7 @@ def test_local_attention_matches_reference(n, b, d, prev, dtype):
 
 @pytest.mark.parametrize("prev", [False, True])
 def test_local_tc_many_units_per_cta(prev):
-    """The tensor-core local kernels are persistent: with ~1,000 units of 128 rows every
+    """The tensor-core local forward is persistent: with ~1,000 units of 128 rows every
     CTA runs several, so shared-memory stages and TMEM buffers are reused."""
     torch.manual_seed(11)
     b, d, heads, n, start = 16, 64, 16, 4100, 32
