@@ -58,8 +58,8 @@ using namespace sm100;
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBuckets = 256;
-constexpr int kReduceThreads = 512;
-constexpr int kLoads = 8;        // 16-byte loads in flight per thread in grad_reduce_kernel
+constexpr int kReduceThreads = 256;
+constexpr int kLoads = 16;       // 16-byte loads in flight per thread in grad_reduce_kernel
 // Flag-slot layout (32-bit words, identical on every rank):
 //   [b * 8 + s]            rank s arrived at bucket b (epoch)
 //   [kFin + s]             rank s finished the step's reduction (epoch)
@@ -127,8 +127,9 @@ grad_reduce_kernel(PeerF32 grads, PeerFlags flags, int rank, int64_t s0, int64_t
   if (!wait_all(flags.p[rank] + bucket * 8, W, epoch, timeout_ns, err)) return;
   // Every thread keeps kLoads 16-byte loads in flight (U vectors from each of
   // the W ranks) before it adds anything: a peer load takes microseconds over
-  // NVLink, and with one vector per rank 32 CTAs kept only ~256 KB in flight
-  // at W = 2 (about 110 GB/s). The ranks are still added in rank order.
+  // NVLink, so the bandwidth follows the bytes in flight. One vector per rank
+  // and thread (32 CTAs of 512 threads) reached about 110 GB/s at W = 2,
+  // eight about 290 GB/s. The ranks are still added in rank order.
   constexpr int U = kLoads / W > 0 ? kLoads / W : 1;
   float acc = 0.f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kReduceThreads;

@@ -308,7 +308,7 @@ class PeerGradBuckets(_BucketCountdown):
     which leaves the global squared gradient norm in ``hyper[3]``.
     """
 
-    CTAS = 32
+    CTAS = 64      # CTAs of 256 threads per bucket kernel (it shares the SMs with the backward)
 
     def __init__(self, flat: FlatParameters, shard: bool, bucket_bytes: int = 32 << 20):
         if flat.heap is None:
