@@ -45,6 +45,9 @@ constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.f;   // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+// log2 of the gate block size (the largest log2 of a block's sum of 2^(a - max)).
+template <int B>
+constexpr float kLog2B = B == 16 ? 4.f : B == 32 ? 5.f : B == 64 ? 6.f : B == 128 ? 7.f : B == 8 ? 3.f : 10.f;
 
 template <int D>
 struct alignas(1024) TcSmem {
@@ -249,8 +252,17 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         // Fast path (most tiles of a long sequence): block log-masses from
         // raw scores with the scale folded into one FFMA per exponent.
         const bool row_ok = pos >= 0;
-        float seg_max[kSeg], seg_lse[kSeg];
-        float tz = kNegInf, remote_max = kNegInf;
+        // Per block g: ms = its maximum (scaled), sum = sum of 2^(a - ms), so
+        // its log-mass is s_g = ms + log2(sum). Everything below is expressed
+        // through ms and sum, which keeps the multi-function unit at one exp2
+        // per score plus two per block (no per-block log2):
+        //   remote weight factor 2^(ms + s_g - m_r) = sum * 2^(2 ms - m_r),
+        //   denominator term     2^(2 s_g - m_r)    = factor * sum,
+        //   log Z_R of the tile  = M + log2(sum_g sum * 2^(ms - M)), M = max ms,
+        //   stabiliser           2 ms + log2(B) >= ms + s_g  (an upper bound
+        //                        is enough: it only shifts the scale of P).
+        float seg_max[kSeg], seg_sum[kSeg];
+        float tile_max = kNegInf, remote_max = kNegInf;
 #pragma unroll
         for (int g = 0; g < kSeg; ++g) {
           float m = e[g * B];
@@ -265,12 +277,17 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
             sum += x;
           }
           seg_max[g] = ms;
-          seg_lse[g] = ms + lg2(sum);
-          tz = log2_add(tz, seg_lse[g]);
-          remote_max = fmaxf(remote_max, ms + seg_lse[g]);
+          seg_sum[g] = sum;
+          tile_max = fmaxf(tile_max, ms);
+          remote_max = fmaxf(remote_max, 2.f * ms + kLog2B<B>);
         }
-        if (!row_ok) {
-          tz = kNegInf;
+        float tz = kNegInf;
+        if (row_ok) {
+          float mass = 0.f;
+#pragma unroll
+          for (int g = 0; g < kSeg; ++g) mass += seg_sum[g] * ex2(seg_max[g] - tile_max);
+          tz = tile_max + lg2(mass);
+        } else {
           remote_max = kNegInf;
         }
         zr = log2_add(zr, tz);
@@ -302,8 +319,8 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         float fr[kSeg];
 #pragma unroll
         for (int g = 0; g < kSeg; ++g) {
-          fr[g] = row_ok ? ex2(seg_max[g] + seg_lse[g] - m_r) : 0.f;
-          if (row_ok) d_r += ex2(2.f * seg_lse[g] - m_r);
+          fr[g] = row_ok ? seg_sum[g] * ex2(2.f * seg_max[g] - m_r) : 0.f;
+          d_r += fr[g] * seg_sum[g];
         }
 #pragma unroll
         for (int c0 = 0; c0 < kN; c0 += 32) {

@@ -96,11 +96,11 @@ layer_norm_bwd_dwdb_kernel(const TGrad* __restrict__ dy, const TIn* __restrict__
 }
 
 // out_p[c] (+)= sum over s of part_p[s][c] for one or two partial arrays
-// (p < kParts). A CTA owns 32 columns; its 8 warps each sum a contiguous
+// (p < kParts). A CTA owns 32 columns; its 16 warps each sum a contiguous
 // slice of the partial rows (a warp reads 128 contiguous bytes per row), and
-// warp 0 adds the 8 slice sums in slice order, so the result does not depend
+// warp 0 adds the 16 slice sums in slice order, so the result does not depend
 // on scheduling. `accumulate` adds into the outputs (parameter gradients).
-constexpr int kReduceSlices = 8;
+constexpr int kReduceSlices = 16;   // 16 warps: each thread has at most splits / 16 loads in flight
 
 template <int kParts>
 __global__ void __launch_bounds__(32 * kReduceSlices)
