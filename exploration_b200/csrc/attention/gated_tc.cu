@@ -1,21 +1,27 @@
 // Exact block-gated attention forward on the 5th-generation tensor cores.
 //
 // One CTA = 128 query rows of one (batch, head); key tiles of 128.
-// Warp roles (256 threads):
-//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring
+// Warp roles (352 threads for gate blocks of at most 64 keys, else 224):
+//   warp 0      TMA producer: Q once, then K/V tiles into a 4-stage ring
+//               (2 stages for head dim 128)
 //   warp 1      MMA issuer (one thread): S = Q K^T into TMEM (double
 //               buffered), then O_r += P_r V and O_l += P_l V with P read
 //               straight from TMEM (tcgen05.mma A-from-TMEM form)
 //   warp 2      TMEM allocator (512 columns)
-//   warps 4-7   softmax/gate warpgroup: thread i owns query row i (TMEM
-//               lane i) and its 128 scores of the current tile
+//   warps 3-6   softmax/gate warpgroup(s): thread i owns query row i (TMEM
+//   (and 7-10)  lane i); with two warpgroups each takes 64 of the tile's 128
+//               score columns, so two warps per SM sub-partition work
+//               through the per-score arithmetic (one warp per
+//               sub-partition was latency-bound: the tile's chain of
+//               dependent exp2 / max / sum steps left issue slots idle)
 //
 // Gate math per row in base-2 units: with a = q.k * scale * log2(e), a
 // block's log-mass is s_j = log2 sum 2^a over its b keys. One exp2 per
 // score (e = 2^(a - blockmax)) serves the block sum, the remote probability
 // p_r = e * 2^(blockmax + s_j - m_r) and the local one p_l = e *
 // 2^(blockmax - m_l); the remote denominator gains 2^(2 s_j - m_r) per block
-// and log Z_R accumulates the blocks' s_j. Both online-softmax states keep a
+// and log Z_R accumulates the blocks' s_j. Statistics that span the whole
+// tile are combined across the two warpgroups once per tile. Both online-softmax states keep a
 // stale maximum unless it grows by more than 2^8 (then O is rescaled in
 // TMEM), so the MMA and softmax warps rarely wait on each other.
 //
@@ -39,8 +45,6 @@ using namespace sm100;
 
 constexpr int kM = 128;          // query rows per CTA
 constexpr int kN = 128;          // keys per tile
-constexpr int kStages = 2;
-constexpr int kThreads = 256;
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.f;   // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
@@ -51,6 +55,12 @@ constexpr float kLog2B = B == 16 ? 4.f : B == 32 ? 5.f : B == 64 ? 6.f : B == 12
 
 template <int D>
 struct alignas(1024) TcSmem {
+  // K/V ring depth. A key tile is one MMA-and-softmax step of well under a
+  // microsecond, while its TMA load (from L2 or HBM) takes longer; with two
+  // stages the step waited for the load of the tile two ahead (head dim 64:
+  // 2.4 us per tile step at the training shape). Head dim 128 keeps two
+  // stages (64 KB each).
+  static constexpr int kStages = D == 64 ? 4 : 2;
   __nv_bfloat16 q[kM * D];
   __nv_bfloat16 k[kStages][kN * D];
   __nv_bfloat16 v[kStages][kN * D];
@@ -60,9 +70,11 @@ struct alignas(1024) TcSmem {
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t o_done;
+  uint64_t xch_bar[2];
   uint32_t tmem_base;
   int abort;
   int pos[kM];
+  float xch[2][2][4][kM];   // [round parity][warpgroup][value][row]: row statistics swapped per tile
 };
 
 struct TcParams {
@@ -83,8 +95,20 @@ EB_DEVICE float log2_add(float a, float b) {
   return m + lg2(ex2(a - m) + ex2(b - m));
 }
 
+// Softmax warpgroups per CTA: two share each row when a gate block fits in
+// half a key tile, one otherwise.
+template <int B>
+constexpr int kSplitFor = B <= 64 ? 2 : 1;
+// Warps 0-2 are the producer, the MMA issuer and the TMEM owner; softmax warp
+// s is hardware warp 3 + s, so it reaches TMEM lanes 32 * ((3 + s) % 4) and
+// each group of four covers all 128 rows. (No idle fourth control warp: with
+// two softmax warpgroups that leaves each thread 184 registers instead of 168.)
+template <int B>
+constexpr int kThreadsFor = 96 + 128 * kSplitFor<B>;
+constexpr int kFirstSoftmaxWarp = 3;
+
 template <int D, int B>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsFor<B>, 1)
 gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, TcParams p) {
   extern __shared__ __align__(1024) uint8_t raw_smem[];
@@ -92,7 +116,11 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       (reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr int kHalves = D / 64;
   constexpr int kBox = 128 * 64;                 // elements per TMA box
-  constexpr int kSeg = kN / B;                   // gate blocks per key tile
+  constexpr int kStages = TcSmem<D>::kStages;
+  constexpr int kSplit = kSplitFor<B>;
+  constexpr int kCols = kN / kSplit;             // score columns per softmax warpgroup
+  constexpr int kSegW = kCols / B;               // gate blocks per softmax warpgroup
+  constexpr int kOCols = D / kSplit;             // accumulator columns each warpgroup rescales and stores
   const int q_tile = gridDim.x - 1 - blockIdx.x; // heaviest (latest) tiles first
   const int head = blockIdx.y, batch = blockIdx.z;
   const int q0 = q_tile * kM;
@@ -107,15 +135,16 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.p_full[s], 128);
+      mbar_init(&sm.p_full[s], 128 * kSplit);
+      mbar_init(&sm.xch_bar[s], 128 * kSplit);
     }
     mbar_init(&sm.o_done, 1);
     sm.abort = 0;
     fence_barrier_init();
   }
   if (warp == 2) tmem_alloc(&sm.tmem_base, kTmemCols);
-  if (threadIdx.x >= 128) {
-    const int row = threadIdx.x - 128;
+  if (threadIdx.x < kM) {
+    const int row = threadIdx.x;
     sm.pos[row] = (q0 + row < p.queries) ? p.pos[static_cast<int64_t>(batch) * p.queries + q0 + row] : -1;
   }
   tc_fence_before();
@@ -214,23 +243,76 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         tc_commit(&sm.o_done);
       }
     }
-  } else if (warp >= 4) {
-    const int row = threadIdx.x - 128;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
+  } else if (warp >= kFirstSoftmaxWarp) {
+    // Softmax/gate warpgroups. With kSplit = 2 (gate blocks of at most 64
+    // keys) two warpgroups share every query row (TMEM lane): warpgroup grp
+    // owns score columns [grp * 64, grp * 64 + 64) of each tile, half of the
+    // accumulator columns for rescaling and the epilogue, and partial
+    // denominators; once per tile they swap the row statistics that span the
+    // whole tile (tile maximum and mass, remote and local maxima) through
+    // shared memory, so both take identical rescaling decisions. Every P
+    // write follows that swap, i.e. both halves of S are already in registers
+    // when either warpgroup overwrites S with P.
+    const int grp = (warp - kFirstSoftmaxWarp) >> 2;
+    const int row = (warp & 3) * 32 + lane;       // TMEM lane of this thread
+    const int col0 = grp * kCols;                 // first key column of the tile owned here
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int pos = sm.pos[row];
     const int pb = pos >= 0 ? pos / B : 0;
     const int first_local = (pb - 1) * B;
-    // Zero both accumulators (the MMAs always accumulate).
+    int round = 0;
+    // Sends this warpgroup's four row values and receives the other's (bounded wait).
+    auto swap = [&](const float (&mine)[4], float (&other)[4]) -> bool {
+      if constexpr (kSplit == 1) {
+        return true;
+      } else {
+        const int slot = round & 1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sm.xch[slot][grp][k][row] = mine[k];
+        tc_fence_before();
+        mbar_arrive(&sm.xch_bar[slot]);
+        const bool done = __all_sync(0xffffffffu, mbar_wait(&sm.xch_bar[slot], (round >> 1) & 1, abort, p.err,
+                                                            kSiteSFull));
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) other[k] = sm.xch[slot][grp ^ 1][k][row];
+        ++round;
+        return done;
+      }
+    };
+    // Zero this warpgroup's share of both accumulators (the MMAs always accumulate).
     {
       uint32_t zero[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) zero[i] = 0u;
 #pragma unroll
-      for (int c = 0; c < 2 * D; c += 32) tmem_st32(lane_addr + 256 + c, zero);
+      for (int c = 0; c < kOCols; c += 32) {
+        tmem_st32(lane_addr + 256 + grp * kOCols + c, zero);
+        tmem_st32(lane_addr + 256 + D + grp * kOCols + c, zero);
+      }
       tc_wait_st();
     }
+    // Running row state; d_r and d_l are this warpgroup's partial denominators.
     float m_r = kNegInf, d_r = 0.f, m_l = kNegInf, d_l = 0.f, zr = kNegInf;
     bool ok = true;
+    // Multiplies this warpgroup's share of O_remote by ar and of O_local by al.
+    auto rescale_o = [&](float ar, float al) {
+#pragma unroll
+      for (int c = 0; c < kOCols; c += 32) {
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const float f = part == 0 ? ar : al;
+          if (__all_sync(0xffffffffu, f == 1.f)) continue;   // tcgen05.ld/st are warp-collective
+          uint32_t r[32];
+          const uint32_t addr = lane_addr + 256 + part * D + grp * kOCols + c;
+          tmem_ld32(addr, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+          tmem_st32(addr, r);
+        }
+      }
+    };
     for (int j = 0; j < tiles; ++j) {
       const int buf = j & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[buf], (j >> 1) & 1, abort, p.err, kSiteSFull))) {
@@ -238,33 +320,31 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         break;
       }
       tc_fence_after();
-      float e[kN];
+      float e[kCols];
 #pragma unroll
-      for (int c = 0; c < kN; c += 32) {
+      for (int c = 0; c < kCols; c += 32) {
         uint32_t r[32];
-        tmem_ld32(lane_addr + buf * 128 + c, r);
+        tmem_ld32(lane_addr + buf * 128 + col0 + c, r);
 #pragma unroll
         for (int i = 0; i < 32; ++i) e[c + i] = __uint_as_float(r[i]);
       }
       tc_wait_ld();
-      const int k0 = j * kN;
+      const int k0 = j * kN + col0;               // key index of this warpgroup's first column
       if (pure_remote(j)) {
-        // Fast path (most tiles of a long sequence): block log-masses from
-        // raw scores with the scale folded into one FFMA per exponent.
-        const bool row_ok = pos >= 0;
-        // Per block g: ms = its maximum (scaled), sum = sum of 2^(a - ms), so
-        // its log-mass is s_g = ms + log2(sum). Everything below is expressed
-        // through ms and sum, which keeps the multi-function unit at one exp2
-        // per score plus two per block (no per-block log2):
+        // Fast path (most tiles of a long sequence). Per block g: ms = its
+        // maximum (scaled), sum = sum of 2^(a - ms), so its log-mass is
+        // s_g = ms + log2(sum). Everything below is expressed through ms and
+        // sum (two exp2 per block, no per-block log2):
         //   remote weight factor 2^(ms + s_g - m_r) = sum * 2^(2 ms - m_r),
         //   denominator term     2^(2 s_g - m_r)    = factor * sum,
         //   log Z_R of the tile  = M + log2(sum_g sum * 2^(ms - M)), M = max ms,
         //   stabiliser           2 ms + log2(B) >= ms + s_g  (an upper bound
         //                        is enough: it only shifts the scale of P).
-        float seg_max[kSeg], seg_sum[kSeg];
+        const bool row_ok = pos >= 0;
+        float seg_max[kSegW], seg_sum[kSegW];
         float tile_max = kNegInf, remote_max = kNegInf;
 #pragma unroll
-        for (int g = 0; g < kSeg; ++g) {
+        for (int g = 0; g < kSegW; ++g) {
           float m = e[g * B];
 #pragma unroll
           for (int c = 1; c < B; ++c) m = fmaxf(m, e[g * B + c]);
@@ -281,21 +361,30 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
           tile_max = fmaxf(tile_max, ms);
           remote_max = fmaxf(remote_max, 2.f * ms + kLog2B<B>);
         }
-        float tz = kNegInf;
-        if (row_ok) {
-          float mass = 0.f;
+        float mass = 0.f;
 #pragma unroll
-          for (int g = 0; g < kSeg; ++g) mass += seg_sum[g] * ex2(seg_max[g] - tile_max);
-          tz = tile_max + lg2(mass);
-        } else {
-          remote_max = kNegInf;
+        for (int g = 0; g < kSegW; ++g) mass += seg_sum[g] * ex2(seg_max[g] - tile_max);
+        if constexpr (kSplit == 2) {
+          const float mine[4] = {tile_max, mass, remote_max, 0.f};
+          float other[4];
+          if (!swap(mine, other)) {
+            ok = false;
+            break;
+          }
+          const float both = fmaxf(tile_max, other[0]);
+          mass = mass * ex2(tile_max - both) + other[1] * ex2(other[0] - both);
+          tile_max = both;
+          remote_max = fmaxf(remote_max, other[2]);
         }
+        float tz = kNegInf;
+        if (row_ok) tz = tile_max + lg2(mass);
+        else remote_max = kNegInf;
         zr = log2_add(zr, tz);
         float alpha_r = 1.f;
         bool rescale = false;
         if (remote_max > m_r + kRescaleThreshold || (m_r == kNegInf && remote_max != kNegInf)) {
           alpha_r = (m_r == kNegInf) ? 0.f : ex2(m_r - remote_max);
-          rescale = d_r > 0.f;
+          rescale = d_r > 0.f || m_r != kNegInf;
           m_r = remote_max;
         }
         if (__any_sync(0xffffffffu, rescale)) {
@@ -305,32 +394,24 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
             break;
           }
           tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < D; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(lane_addr + 256 + c, r);
-            tc_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha_r);
-            tmem_st32(lane_addr + 256 + c, r);
-          }
+          rescale_o(alpha_r, 1.f);
         }
         d_r *= alpha_r;
-        float fr[kSeg];
+        float fr[kSegW];
 #pragma unroll
-        for (int g = 0; g < kSeg; ++g) {
+        for (int g = 0; g < kSegW; ++g) {
           fr[g] = row_ok ? seg_sum[g] * ex2(2.f * seg_max[g] - m_r) : 0.f;
           d_r += fr[g] * seg_sum[g];
         }
 #pragma unroll
-        for (int c0 = 0; c0 < kN; c0 += 32) {
+        for (int c0 = 0; c0 < kCols; c0 += 32) {
           uint32_t packed_r[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int c = c0 + 2 * i;
             packed_r[i] = pack_bf16(e[c] * fr[c / B], e[c + 1] * fr[(c + 1) / B]);
           }
-          tmem_st16(lane_addr + buf * 128 + c0 / 2, packed_r);
+          tmem_st16(lane_addr + buf * 128 + (col0 + c0) / 2, packed_r);
         }
         tc_wait_st();
         tc_fence_before();
@@ -340,15 +421,15 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       // Scaled base-2 logits; keys past N are -inf.
       float local_max = kNegInf;
 #pragma unroll
-      for (int c = 0; c < kN; ++c) {
+      for (int c = 0; c < kCols; ++c) {
         const int key = k0 + c;
         e[c] = key < p.keys ? e[c] * p.scale_log2 : kNegInf;
         const bool loc = pos >= 0 && key >= first_local && key <= pos;
         if (loc) local_max = fmaxf(local_max, e[c]);
       }
-      float seg_max[kSeg], seg_lse[kSeg];
+      float seg_max[kSegW], seg_lse[kSegW];
 #pragma unroll
-      for (int g = 0; g < kSeg; ++g) {
+      for (int g = 0; g < kSegW; ++g) {
         float m = kNegInf;
 #pragma unroll
         for (int c = 0; c < B; ++c) m = fmaxf(m, e[g * B + c]);
@@ -365,24 +446,35 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       // Remote blocks: log Z_R and the remote maximum.
       float tz = kNegInf, remote_max = kNegInf;
 #pragma unroll
-      for (int g = 0; g < kSeg; ++g) {
+      for (int g = 0; g < kSegW; ++g) {
         const bool rem = pos >= 0 && (k0 / B + g) < pb - 1;
         if (rem && seg_lse[g] != kNegInf) {
           tz = log2_add(tz, seg_lse[g]);
           remote_max = fmaxf(remote_max, seg_max[g] + seg_lse[g]);
         }
       }
+      if constexpr (kSplit == 2) {
+        const float mine[4] = {tz, remote_max, local_max, 0.f};
+        float other[4];
+        if (!swap(mine, other)) {
+          ok = false;
+          break;
+        }
+        tz = log2_add(tz, other[0]);
+        remote_max = fmaxf(remote_max, other[1]);
+        local_max = fmaxf(local_max, other[2]);
+      }
       zr = log2_add(zr, tz);
       bool rescale = false;
       float alpha_r = 1.f, alpha_l = 1.f;
       if (remote_max > m_r + kRescaleThreshold || (m_r == kNegInf && remote_max != kNegInf)) {
         alpha_r = (m_r == kNegInf) ? 0.f : ex2(m_r - remote_max);
-        rescale |= d_r > 0.f;
+        rescale |= d_r > 0.f || m_r != kNegInf;
         m_r = remote_max;
       }
       if (local_max > m_l + kRescaleThreshold || (m_l == kNegInf && local_max != kNegInf)) {
         alpha_l = (m_l == kNegInf) ? 0.f : ex2(m_l - local_max);
-        rescale |= d_l > 0.f;
+        rescale |= d_l > 0.f || m_l != kNegInf;
         m_l = local_max;
       }
       // tcgen05.ld/st are warp-collective: the whole warp rescales when any lane must.
@@ -394,30 +486,21 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2 * D; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(lane_addr + 256 + c, r);
-          tc_wait_ld();
-          const float f = c < D ? alpha_r : alpha_l;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-          tmem_st32(lane_addr + 256 + c, r);
-        }
+        rescale_o(alpha_r, alpha_l);
       }
       d_r *= alpha_r;
       d_l *= alpha_l;
       const bool use_r = remote_used(j), use_l = local_used(j);
-      float fr[kSeg], fl[kSeg];
+      float fr[kSegW], fl[kSegW];
 #pragma unroll
-      for (int g = 0; g < kSeg; ++g) {
+      for (int g = 0; g < kSegW; ++g) {
         const bool rem = pos >= 0 && (k0 / B + g) < pb - 1 && seg_lse[g] != kNegInf;
         fr[g] = rem ? ex2(seg_max[g] + seg_lse[g] - m_r) : 0.f;
         if (rem) d_r += ex2(2.f * seg_lse[g] - m_r);
         fl[g] = (m_l == kNegInf || seg_max[g] == kNegInf) ? 0.f : ex2(seg_max[g] - m_l);
       }
 #pragma unroll
-      for (int c0 = 0; c0 < kN; c0 += 32) {
+      for (int c0 = 0; c0 < kCols; c0 += 32) {
         uint32_t packed_r[16], packed_l[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -431,8 +514,8 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
           d_l += x0 + x1;
           packed_l[i] = pack_bf16(x0, x1);
         }
-        if (use_r) tmem_st16(lane_addr + buf * 128 + c0 / 2, packed_r);
-        if (use_l) tmem_st16(lane_addr + buf * 128 + 64 + c0 / 2, packed_l);
+        if (use_r) tmem_st16(lane_addr + buf * 128 + (col0 + c0) / 2, packed_r);
+        if (use_l) tmem_st16(lane_addr + buf * 128 + 64 + (col0 + c0) / 2, packed_l);
       }
       tc_wait_st();
       tc_fence_before();
@@ -440,6 +523,14 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     }
     if (ok && tiles > 0) ok = mbar_wait(&sm.o_done, (tiles - 1) & 1, abort, p.err, kSiteODone);
     ok = __all_sync(0xffffffffu, ok);
+    if constexpr (kSplit == 2) {
+      // Whole-row denominators from the two partial sums.
+      const float mine[4] = {d_r, d_l, 0.f, 0.f};
+      float other[4] = {0.f, 0.f, 0.f, 0.f};
+      ok = swap(mine, other) && ok;
+      d_r += other[0];
+      d_l += other[1];
+    }
     tc_fence_after();
     const int qrow = q0 + row;
     const bool write = qrow < p.queries;
@@ -453,7 +544,7 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       const float wr = (ok && d_r > 0.f) ? prob_r / d_r : 0.f;
       const float wl = (ok && d_l > 0.f) ? prob_l / d_l : 0.f;
       const int64_t s = (static_cast<int64_t>(batch) * p.queries + (write ? qrow : 0)) * p.heads + head;
-      if (write) {
+      if (write && grp == 0) {
         p.pr[s] = prob_r;
         p.zr[s] = zr == kNegInf ? kNegInf : zr * kLn2;
         p.lse[s] = total == kNegInf ? kNegInf : total * kLn2;
@@ -461,7 +552,7 @@ gated_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       __nv_bfloat16* orow = p.out + s * D;
       float* rrow = p.rc + s * D;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      for (int c = grp * kOCols; c < (grp + 1) * kOCols; c += 32) {
         uint32_t rr[32], ll_[32];
         tmem_ld32(lane_addr + 256 + c, rr);
         tmem_ld32(lane_addr + 256 + D + c, ll_);
@@ -504,7 +595,7 @@ void launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const
   auto kernel = gated_fwd_tc_kernel<D, B>;
   EB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid((queries + kM - 1) / kM, heads, batch);
-  kernel<<<grid, kThreads, smem, stream>>>(tq, tk, tv, params);
+  kernel<<<grid, kThreadsFor<B>, smem, stream>>>(tq, tk, tv, params);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch(1);
 }

@@ -334,11 +334,15 @@ EB_DEVICE void finish_stats(RowStats& st) {
 
 template <int D>
 struct alignas(1024) DqSmem {
+  // K/V ring depth: four stages at head dim 64 so that the loads of the next
+  // tiles are in flight while a tile's MMAs and gradient arithmetic run; two
+  // at head dim 128 (64 KB per stage).
+  static constexpr int kStagesKV = D == 64 ? 4 : 2;
   __nv_bfloat16 q[kT * D];
   __nv_bfloat16 g[kT * D];
-  __nv_bfloat16 k[2][kT * D];
-  __nv_bfloat16 v[2][kT * D];
-  uint64_t qg_full, kv_full[2], kv_empty[2], sdp_full, da_full, dq_done;
+  __nv_bfloat16 k[kStagesKV][kT * D];
+  __nv_bfloat16 v[kStagesKV][kT * D];
+  uint64_t qg_full, kv_full[kStagesKV], kv_empty[kStagesKV], sdp_full, da_full, dq_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -355,6 +359,7 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
   extern __shared__ __align__(1024) uint8_t raw_smem[];
   DqSmem<D>& sm = *reinterpret_cast<DqSmem<D>*>(
       (reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int kS = DqSmem<D>::kStagesKV;
   constexpr int kHalves = D / 64, kBox = 128 * 64;
   // dA (bf16) lives in its own TMEM columns when two warpgroups write it
   // concurrently (one warpgroup's dA may not overwrite the other's S).
@@ -366,7 +371,7 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
   volatile int* abort = &sm.abort;
   if (threadIdx.x == 0) {
     mbar_init(&sm.qg_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
@@ -394,8 +399,8 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       }
       int issued = 0;
       for (int j = 0; j < tiles; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&sm.kv_empty[s], ((j >> 1) - 1) & 1, abort, p.err, kSiteKvEmpty)) break;
+        const int s = j % kS;
+        if (j >= kS && !mbar_wait(&sm.kv_empty[s], ((j / kS) - 1) & 1, abort, p.err, kSiteKvEmpty)) break;
         mbar_expect_tx(&sm.kv_full[s], 2 * kT * D * 2);
         for (int h = 0; h < kHalves; ++h) {
           tma_load_4d(sm.k[s] + h * kBox, &tk, &sm.kv_full[s], h * 64, head, j * kT, batch);
@@ -404,8 +409,8 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
         ++issued;
       }
       if (*abort) {
-        for (int j = max(0, issued - 2); j < issued; ++j)
-          mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1, abort, nullptr, kSiteDrain);
+        for (int j = max(0, issued - kS); j < issued; ++j)
+          mbar_wait(&sm.kv_full[j % kS], (j / kS) & 1, abort, nullptr, kSiteDrain);
         mbar_wait(&sm.qg_full, 0, abort, nullptr, kSiteDrain);
       }
     }
@@ -416,8 +421,8 @@ gated_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       const uint32_t q_addr = smem_u32(sm.q), g_addr = smem_u32(sm.g);
       bool ok = mbar_wait(&sm.qg_full, 0, abort, p.err, kSiteQFull);
       for (int j = 0; ok && j < tiles; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&sm.kv_full[s], (j >> 1) & 1, abort, p.err, kSiteKvFull)) break;
+        const int s = j % kS;
+        if (!mbar_wait(&sm.kv_full[s], (j / kS) & 1, abort, p.err, kSiteKvFull)) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[s]), v_addr = smem_u32(sm.v[s]);
 #pragma unroll
